@@ -1,0 +1,477 @@
+"""Benchmark of the NVFP4-KV decode attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload auto|c2|c3_32k|c3_131k|c4|c5]
+
+Default workload ("auto"): one decode step = q_len 1 attention over 16
+attention layers, each with independent seeded NVFP4 KV of 65,536 tokens per
+GPU (BASELINE config 2 at N=1).  At N > 1 the 16 sequences are 65,536*N
+tokens long and sharded contiguously by pages (N=4 is the 262,144-token
+native context of config 4): per layer every rank appends (the owner
+writes), computes its shard's (m, l, O) record, all-gathers the records over
+NCCL and LSE-combines them — "scaling": "weak" (per-GPU work fixed).
+
+value  = whole-job algorithmic HBM bytes per step / device step time (GB/s);
+         per layer 1152*L + 2*(24*256*2) + 4*P + 1152 + 2*4*256*2 bytes.
+e2e    = the same bytes through the public API `qwarz_b200.attention.attend`
+         with every step's Q/K/V copied in from pinned host memory and the
+         outputs copied back, all inside the timed region.
+roofline: the split kernel alone (graph of its 16 launches), CUDA events.
+Inputs: synthetic, seeded, BF16 ~N(0,1) with 4 outlier channels x8 (K, V)
+quantised to NVFP4 by the library's own writer; 16 layers x 75.5 MB of KV
+rotate through the step, so every layer's pages are evicted from the 126 MB
+L2 before they are read again.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HEADS, KV_HEADS, DIM, PAGE = 24, 4, 256, 256
+LAYERS = 16
+TOKENS_PER_GPU = 65536
+METRIC = "NVFP4-KV decode attn µs/step & HBM GB/s vs ~8 TB/s, 64K–262K ctx, 1–8 B200"
+
+
+def layer_bytes(L: int, q_len: int = 1, pages: int | None = None) -> int:
+    """Algorithmic HBM bytes of one layer call (KV codes+scales, Q in, O out,
+    table, append write, new K/V read)."""
+    P = pages if pages is not None else math.ceil(L / PAGE)
+    return 1152 * L + 2 * (q_len * HEADS * DIM * 2) + 4 * P + 1152 * q_len + 2 * q_len * KV_HEADS * DIM * 2
+
+
+def peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every 100 ms."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4, "gpu_idle": 0x1,
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.nvml is not None:
+            self._stop.set()
+            self.thread.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------- data
+def build_layer(ops, device, pages: int, tokens: int, seed: int, dtype=torch.bfloat16):
+    """One layer's NVFP4 cache: `tokens` seeded K/V rows written by the
+    library's writer into `pages` pages in a seed-permuted order."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    perm = torch.randperm(pages, generator=g, device=device).to(torch.int32)
+    cache = (torch.zeros(pages, PAGE, KV_HEADS, DIM // 2, dtype=torch.uint8, device=device),
+             torch.zeros(pages, PAGE, KV_HEADS, DIM // 2, dtype=torch.uint8, device=device),
+             torch.zeros(pages, PAGE, KV_HEADS, DIM // 16, dtype=torch.float8_e4m3fn, device=device),
+             torch.zeros(pages, PAGE, KV_HEADS, DIM // 16, dtype=torch.float8_e4m3fn, device=device))
+    outl = torch.randperm(DIM, generator=g, device=device)[:4]
+    zero = torch.zeros(1, dtype=torch.int32, device=device)
+    chunk = 16384
+    for t0 in range(0, tokens, chunk):
+        n = min(chunk, tokens - t0)
+        k = torch.randn(n, KV_HEADS, DIM, generator=g, device=device)
+        v = torch.randn(n, KV_HEADS, DIM, generator=g, device=device)
+        k[..., outl] *= 8
+        v[..., outl] *= 8
+        start = torch.full((1,), t0, dtype=torch.int32, device=device)
+        ops.nvfp4_append(k.to(dtype).contiguous(), v.to(dtype).contiguous(), *cache, perm, start)
+    del zero
+    return cache, perm
+
+
+def cuda_time(fn, iters: int, stream) -> float:
+    """Total milliseconds of `iters` calls of fn, CUDA events on `stream`."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(iters):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+# ------------------------------------------------------------- CPU oracle
+def cpu_oracle_sample(layers_cpu, tokens: int, seconds: float = 15.0):
+    """Time the oracle port (dequant gather + FP32 attention) on host cores
+    over whole layers of the workload until ~`seconds` of CPU work."""
+    from oracle import attention as oatt
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        cache, table, q = layers_cpu[done % len(layers_cpu)]
+        oatt.nvfp4_attention(q.float(), cache[0], cache[1], cache[2].view(torch.uint8),
+                             cache[3].view(torch.uint8), table, tokens - 1)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 64:
+            break
+    per_layer_s = el / done
+    return {
+        "value": layer_bytes(tokens) / per_layer_s / 1e9,
+        "unit": "GB/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"{done} layer call(s) of the {tokens}-token q_len=1 decode (NVFP4 dequant gather "
+                  f"+ FP32 softmax attention, torch CPU), {el:.1f} s, {per_layer_s * 1e3:.1f} ms/layer",
+    }
+
+
+def cpu_layers_for_oracle(device_layers, queries, n: int):
+    out = []
+    for i in range(n):
+        cache, table = device_layers[i]
+        out.append((tuple(t.cpu() for t in cache), table.cpu(), queries[i].float().cpu()))
+    return out
+
+
+# -------------------------------------------------------------- our arm
+def run_ours(args, rank: int, world: int, device) -> dict | None:
+    from qwarz_b200 import attention as qattn
+    from qwarz_b200 import build, ops, sharded
+
+    build.build()
+    torch.cuda.set_device(device)
+    stream = torch.cuda.current_stream(device)
+    tokens_total = TOKENS_PER_GPU * world
+    pages_total = tokens_total // PAGE
+    shards = sharded.shard_pages(pages_total, world)
+    shard = shards[rank]
+    local_pages = shard.num_pages
+    local_tokens = shard.tok_span
+    dtype = torch.bfloat16
+
+    layers = []
+    for l in range(LAYERS):
+        cache, perm = build_layer(ops, device, local_pages, local_tokens, seed=1000 * rank + l)
+        layers.append((cache, perm))
+    g = torch.Generator(device=device).manual_seed(4242)
+    q = [torch.randn(1, 1, HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(LAYERS)]
+    knew = [torch.randn(1, 1, KV_HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(LAYERS)]
+    vnew = [torch.randn(1, 1, KV_HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(LAYERS)]
+    out = [torch.empty(1, 1, HEADS, DIM, dtype=dtype, device=device) for _ in range(LAYERS)]
+    pre = torch.tensor([tokens_total - 1], dtype=torch.int32, device=device)
+    torch.cuda.synchronize()
+
+    splits = ops.default_splits(device, local_tokens, 1)
+    if world == 1:
+        po, pml = ops.split_workspace(device, 1, splits)
+
+        def step():
+            for l in range(LAYERS):
+                cache, perm = layers[l]
+                ops.nvfp4_attend(q[l], knew[l], vnew[l], *cache, perm, pre, out[l], po, pml, splits)
+
+        def split_only():
+            for l in range(LAYERS):
+                cache, perm = layers[l]
+                ops.attn_split(q[l], cache[0], cache[1], perm, pre, po, pml, cache[2], cache[3], splits)
+    else:
+        dec = sharded.ShardedDecode(shard, device, 1, splits)
+
+        def step():
+            for l in range(LAYERS):
+                cache, perm = layers[l]
+                dec.step(q[l], knew[l], vnew[l], cache, perm, pre, out[l])
+
+        def split_only():
+            for l in range(LAYERS):
+                cache, perm = layers[l]
+                dec.partial(q[l], cache, perm, pre)
+
+    def capture(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        torch.cuda.synchronize()
+        return graph
+
+    graph = capture(step)
+    split_graph = capture(split_only)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[device.index])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    with ClockSampler(device.index) as clocks:
+        t_ms = cuda_time(graph.replay, args.steps, torch.cuda.current_stream(device))
+        barrier()
+        t_split_ms = cuda_time(split_graph.replay, args.steps, torch.cuda.current_stream(device))
+        barrier()
+    ms_step = t_ms / args.steps
+    split_ms_launch = t_split_ms / args.steps / LAYERS
+
+    # ----- end to end through the public API, host copies inside the graph
+    e2e_ms = None
+    h2d = LAYERS * (q[0].numel() + knew[0].numel() + vnew[0].numel()) * 2
+    d2h = LAYERS * out[0].numel() * 2
+    if world == 1:
+        host_q = [t.cpu().pin_memory() for t in q]
+        host_k = [t.cpu().pin_memory() for t in knew]
+        host_v = [t.cpu().pin_memory() for t in vnew]
+        host_o = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in out]
+        dq = [torch.empty_like(t) for t in q]
+        dk = [torch.empty_like(t) for t in knew]
+        dv = [torch.empty_like(t) for t in vnew]
+
+        tables = [layers[l][1].view(1, -1) for l in range(LAYERS)]
+
+        def e2e_step():
+            for l in range(LAYERS):
+                dq[l].copy_(host_q[l], non_blocking=True)
+                dk[l].copy_(host_k[l], non_blocking=True)
+                dv[l].copy_(host_v[l], non_blocking=True)
+                res = qattn.attend(dq[l], dk[l], dv[l], layers[l][0], pre, block_table=tables[l])
+                host_o[l].copy_(res, non_blocking=True)
+
+        qattn.release_attention_plans()
+        e2e_graph = capture(e2e_step)
+        for _ in range(args.warmup):
+            e2e_graph.replay()
+        torch.cuda.synchronize()
+        e2e_ms = cuda_time(e2e_graph.replay, args.steps, torch.cuda.current_stream(device)) / args.steps
+        del e2e_graph
+
+    # ----- aggregate over ranks
+    bytes_rank = LAYERS * layer_bytes(local_tokens, 1, local_pages)
+    if world > 1:
+        t = torch.tensor([ms_step, split_ms_launch], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_step, split_ms_launch = float(t[0]), float(t[1])
+    del graph, split_graph
+    if rank != 0:
+        return None
+
+    total_bytes = bytes_rank * world
+    pk, pk_kind = peaks()
+    achieved = layer_bytes(local_tokens, 1, local_pages) / (split_ms_launch * 1e-3) / 1e9
+    traffic = None
+    tr_path = ROOT / "profiles" / "decode_traffic.json"
+    if tr_path.exists():
+        try:
+            traffic = json.loads(tr_path.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    result = {
+        "metric": METRIC,
+        "value": total_bytes / (ms_step * 1e-3) / 1e9,
+        "unit": "GB/s",
+        "us_per_step": ms_step * 1e3,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 Q/K/V/O; NVFP4 (E2M1 + E4M3/16) KV; f16 tensor-core MMA, f32 softmax/accumulate",
+        "data": "synthetic (seeded BF16 N(0,1) K/V with 4 outlier channels x8, NVFP4-quantised by "
+                "the library writer; BF16 N(0,1) Q)",
+        "config": {
+            "workload": ("C2: decode q_len=1, 16 attention layers x 65,536 tokens NVFP4 KV "
+                         "(256 pages of 256, seed-permuted tables), GQA 24/4 x 256"
+                         if world == 1 else
+                         f"weak-scaled C4: decode q_len=1, 16 layers x {tokens_total} tokens "
+                         f"sharded over {world} GPUs ({TOKENS_PER_GPU} per GPU), NCCL all-gather "
+                         "of (m,l,O) + LSE combine"),
+            "layers": LAYERS, "context_tokens": tokens_total, "tokens_per_gpu": local_tokens,
+            "q_len": 1, "heads": "24q/4kv", "head_dim": DIM, "page": PAGE, "splits_per_head": splits,
+            "l2": "inputs larger than L2: 16 layers x 75.5 MB KV rotate per step",
+            "graph": "one CUDA graph per step",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "nvfp4_decode_kernel (split-K, one launch per layer)",
+            "achieved": achieved,
+            "peak": pk["hbm_gbs"],
+            "peak_kind": pk_kind,
+            "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"],
+            "traffic": traffic,
+            "us_per_launch": split_ms_launch * 1e3,
+            "algorithmic_bytes_per_launch": layer_bytes(local_tokens, 1, local_pages),
+        },
+        "e2e": None if e2e_ms is None else {
+            "value": total_bytes / (e2e_ms * 1e-3) / 1e9,
+            "unit": "GB/s",
+            "us_per_step": e2e_ms * 1e3,
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "api": "qwarz_b200.attention.attend per layer, pinned H2D/D2H, captured in one CUDA graph",
+        },
+        "gpu_launches": args.steps * LAYERS * 3 + args.steps * LAYERS,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        sample = cpu_layers_for_oracle(layers, [t.view(1, HEADS, DIM) for t in q], 2)
+        result["cpu_baseline"] = cpu_oracle_sample(sample, local_tokens, args.cpu_seconds)
+    return result
+
+
+# --------------------------------------------------------- reference arm
+def run_reference(args) -> dict:
+    """The reference's CPU oracle path, restated (oracle/), on host cores:
+    NVFP4 -> dequant gather (xqa.py:73-143) + FP32 softmax attention
+    (xqa.py:612-673), one 65,536-token layer call per step."""
+    import numpy as np
+    from oracle import attention as oatt
+    from oracle import nvfp4
+    from tests.golden import cases
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    tokens = TOKENS_PER_GPU
+    pages = tokens // PAGE
+    layers = []
+    for l in range(2):
+        k = cases.kv_rows(900 + l, tokens)
+        v = cases.kv_rows(950 + l, tokens)
+        kc, ks = nvfp4.quantize_rows(k)
+        vc, vs = nvfp4.quantize_rows(v)
+        perm = np.random.default_rng(l).permutation(pages).astype(np.int32)
+        inv = np.empty_like(perm)
+        inv[perm] = np.arange(pages, dtype=np.int32)
+        def paged(a):
+            a = a.reshape(pages, PAGE, *a.shape[1:])
+            return torch.from_numpy(np.ascontiguousarray(a[inv]))
+        q = torch.randn(1, HEADS, DIM, generator=torch.Generator().manual_seed(l)).bfloat16()
+        layers.append(((paged(kc), paged(vc), paged(ks), paged(vs)), torch.from_numpy(perm), q))
+
+    def one(i):
+        cache, table, q = layers[i % len(layers)]
+        oatt.nvfp4_attention(q.float(), cache[0], cache[1], cache[2], cache[3], table, tokens - 1)
+
+    for i in range(args.warmup):
+        one(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one(i)
+    el = time.perf_counter() - t0
+    per = el / args.steps
+    value = layer_bytes(tokens) / per / 1e9
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "us_per_step": per * 1e6 * LAYERS,
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per * 1e3 * LAYERS,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "NVFP4 KV dequantised to FP32; FP32 softmax attention",
+        "data": "synthetic (seeded N(0,1) K/V with 4 outlier channels x8, NVFP4 by the oracle writer)",
+        "config": {"workload": "C2 sample: one 65,536-token q_len=1 decode layer call per step "
+                               "(ms_per_step scaled to 16 layers)",
+                   "layers_timed_per_step": 1, "context_tokens": tokens},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"{args.steps} layer calls after {args.warmup} warm-up, "
+                                   f"{per * 1e3:.1f} ms per layer call"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        print(json.dumps(run_reference(args)), flush=True)
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    try:
+        result = run_ours(args, rank, world, device)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,195 @@
+/*
+ * qwz_b200 — C ABI of the B200 (sm_100a) NVFP4/FP8 paged-attention kernels.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a cudaStream_t passed as void*;
+ *   - enqueues work on that stream and returns without synchronising;
+ *   - allocates nothing (workspaces are caller-owned), so calls may be
+ *     captured into CUDA graphs;
+ *   - returns 0 on success, QWZ_EINVAL for a rejected argument (nothing was
+ *     launched) or QWZ_ELAUNCH when a launch failed; qwz_last_error() then
+ *     describes the failure (thread-local string).
+ * Device-side metadata faults (a logical page beyond the block table, a
+ * physical page id outside the pool) skip the affected copy/store and set
+ * bits of a device error word that qwz_device_error() reads back.
+ *
+ * Fixed geometry (the reference pins it, src/qwasar_runtime/xqa.py:318-321):
+ * 24 query heads, 4 KV heads, head_dim 256, 256-token pages.
+ * NVFP4 cache (engine/forward/attention.py:159-167): codes uint8
+ * [P, 256, 4, 128] (even d = low nibble), scales E4M3 [P, 256, 4, 16].
+ * Lengths are int32 device words (graph-safe: never read on the host).
+ */
+#ifndef QWZ_B200_H
+#define QWZ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QWZ_OK 0
+#define QWZ_EINVAL (-1)
+#define QWZ_ELAUNCH (-2)
+
+#define QWZ_DTYPE_F16 0
+#define QWZ_DTYPE_BF16 1
+
+/* Bits of the device error word. */
+#define QWZ_DEVERR_TABLE_RANGE 1
+#define QWZ_DEVERR_PAGE_RANGE 2
+#define QWZ_DEVERR_SLOT_RANGE 4
+
+/* Library version string. */
+const char* qwz_version(void);
+
+/* Description of the last error returned on this host thread. */
+const char* qwz_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device error word of the current
+ * device.  Synchronises the device; for tests and diagnostics only. */
+int qwz_device_error(int32_t* out, int32_t clear);
+
+/*
+ * NVFP4 KV-page writer.  Replaces the reference's append
+ * (src/qwasar_runtime/xqa.py:356-379, ExLlamaV3 `_paged_kv_update_nvfp4_kernel`,
+ * same argument order): for i < append_len and each KV head, quantises row i
+ * of k and v ([append_len, num_kv_heads, 256], FP16/BF16) into the page
+ * block_table[pos / 256] at offset pos % 256, pos = cache_seqlens[0] + i.
+ * One E4M3 scale (amax / 6, RNE) per 16 elements; E2M1 codes (RNE of
+ * x / scale, saturating at 6).  num_pages bounds the physical page ids.
+ */
+int qwz_nvfp4_append(const void* k, const void* v, void* k_cache, void* v_cache,
+                     void* k_scales, void* v_scales, const int32_t* block_table,
+                     const int32_t* cache_seqlens, int32_t table_width, int32_t append_len,
+                     int32_t num_kv_heads, int32_t page_size, int32_t head_dim,
+                     int32_t num_pages, int32_t dtype, void* stream);
+
+/*
+ * Writer for one shard of a sequence-sharded cache: as qwz_nvfp4_append, but
+ * block_table entry 0 maps logical page table_page_offset, and rows whose
+ * page lies outside [table_page_offset, table_page_offset + table_width) are
+ * skipped silently (another rank owns them).  New work: the reference has no
+ * multi-GPU path.
+ */
+int qwz_nvfp4_append_shard(const void* k, const void* v, void* k_cache, void* v_cache,
+                           void* k_scales, void* v_scales, const int32_t* block_table,
+                           const int32_t* cache_seqlens, int32_t table_width,
+                           int32_t table_page_offset, int32_t append_len, int32_t num_pages,
+                           int32_t dtype, void* stream);
+
+/*
+ * Split-K attention kernel with the reference split ABI
+ * (tests/test_attention_kernel_abi.py:13-32): arguments 0..14 in the order
+ *   q, k_cache, v_cache, block_table, cache_seqlens, out, partial_o,
+ *   partial_ml, k_scales, v_scales, h32, split_len, num_pages_per_seq,
+ *   num_splits, sinks
+ * then the two trailing pointer slots global_scratch, profile_scratch.
+ * For the NVFP4 cache h32 and sinks must be NULL; out is not written (the
+ * combine writes it); the trailing slots are reserved and may be NULL.
+ *   q            [q_len, 24, 256] FP16/BF16 (q_len 1..8)
+ *   cache_seqlens pre-append length; attention covers post = pre + q_len
+ *                tokens, row (qi, head) sees tokens <= pre + qi
+ *   partial_o    FP32 [q_len, 24, num_splits, 256] (unnormalised O)
+ *   partial_ml   FP32 [q_len, 24, num_splits, 2] (m in log2 units of
+ *                sm_scale * q.k, l); splits that own no token write m = -inf
+ *   split_len    0: the token range is balanced over num_splits on the
+ *                device; > 0: fixed tokens per split (multiple of 256)
+ *   num_pages_per_seq  entries of the block table row
+ *   num_pages    physical pages in the pool (bounds check)
+ * Grid = num_splits x 4 KV heads.
+ */
+int qwz_attn_split(const void* q, const void* k_cache, const void* v_cache,
+                   const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                   float* partial_o, float* partial_ml, const void* k_scales,
+                   const void* v_scales, const void* h32, int32_t split_len,
+                   int32_t num_pages_per_seq, int32_t num_splits, const void* sinks,
+                   void* global_scratch, void* profile_scratch, int32_t q_len,
+                   int32_t num_pages, float sm_scale, int32_t dtype, void* stream);
+
+/*
+ * Combine kernel with the reference combine ABI
+ * (tests/test_attention_kernel_abi.py:22-24): partial_o, partial_ml, out,
+ * h32, num_splits, sinks.  Writes out [q_len, 24, 256] (FP16/BF16),
+ * out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.  h32, sinks NULL.
+ */
+int qwz_attn_combine(const float* partial_o, const float* partial_ml, void* out,
+                     const void* h32, int32_t num_splits, const void* sinks, int32_t q_len,
+                     int32_t dtype, void* stream);
+
+/*
+ * The adapter's decode/verify route in one call: append + split + combine
+ * (replaces NVFP4AttentionAdapter._append + _xqa, src/qwasar_runtime/
+ * xqa.py:356-379 and 484-554).  k, v: the q_len new rows [q_len, 4, 256];
+ * cache_seqlens is the PRE-append length (it is not modified).
+ */
+int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache, void* v_cache,
+                     void* k_scales, void* v_scales, const int32_t* block_table,
+                     const int32_t* cache_seqlens, void* out, float* partial_o,
+                     float* partial_ml, int32_t table_width, int32_t num_pages, int32_t q_len,
+                     int32_t num_splits, float sm_scale, int32_t dtype, void* stream);
+
+/*
+ * Sequence-sharded decode, local half: attention of q over the logical
+ * tokens [tok_begin, tok_begin + tok_span) clipped to the post-append length,
+ * through a block table whose entry 0 maps logical page tok_begin / 256
+ * (tok_begin a multiple of 256).  The local splits are reduced to one
+ * record per row: send_buf FP32 [q_len * 24, 258] = (m, l, O[256]).
+ * New work; the reference has no multi-GPU path (its engine refuses more
+ * than one GPU, src/qwasar_runtime/engine.py:602-610).
+ */
+int qwz_attn_shard_partial(const void* q, const void* k_cache, const void* v_cache,
+                           const void* k_scales, const void* v_scales,
+                           const int32_t* block_table, const int32_t* cache_seqlens,
+                           float* partial_o, float* partial_ml, float* send_buf,
+                           int32_t table_width, int32_t num_pages, int32_t tok_begin,
+                           int32_t tok_span, int32_t q_len, int32_t num_splits, float sm_scale,
+                           int32_t dtype, void* stream);
+
+/*
+ * Sequence-sharded decode, global half: LSE combine of the all-gathered
+ * records gathered FP32 [world, q_len * 24, 258] into out [q_len, 24, 256].
+ */
+int qwz_lse_combine_gathered(const float* gathered, void* out, int32_t world, int32_t q_len,
+                             int32_t dtype, void* stream);
+
+/*
+ * FP8 shadow-KV draft decode (replaces DecodeAttention.attend,
+ * engine/forward/draft_attention.py:93-108): one query row per head,
+ *   q      FP16 [1, 1, 24, 256]
+ *   k8,v8  E4M3 [capacity, 4, 256] (contiguous, not paged)
+ *   k_scale, v_scale FP32 [ceil(capacity/256), 4] per (page, head), or NULL
+ *          (scale 1, the reference's `_fp8` shadow)
+ *   length int32 [1] on the device: keys [0, length) are attended
+ *   part   FP32 [24, splits, 256], stat FP32 [24, splits, 2]
+ *   out    FP16 [1, 1, 24, 256]
+ */
+int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const float* k_scale,
+                         const float* v_scale, const int32_t* length, float* part, float* stat,
+                         void* out, int32_t splits, int32_t capacity, void* stream);
+
+/*
+ * FP8 shadow write (replaces engine/forward/draft.py:359-366): writes one new
+ * row k, v [4, 256] (FP16/BF16) into k8, v8 at slot position[0] as
+ * E4M3(clamp(x / scale, +-448)), scale per (page, head) or 1 when NULL.
+ */
+int qwz_fp8_shadow_write(const void* k, const void* v, void* k8, void* v8, const float* k_scale,
+                         const float* v_scale, const int32_t* position, int32_t capacity,
+                         int32_t dtype, void* stream);
+
+/*
+ * NVFP4 -> FP16 dequant gather in logical order; mirrors the reference
+ * oracle kernel `_gather_nvfp4_kernel` (src/qwasar_runtime/xqa.py:73-143)
+ * argument for argument: out[b, t, h, :] for t < seq_lens[b]; tokens beyond
+ * seq_lens[b] are not written.  head_dim must be a multiple of 16.
+ */
+int qwz_nvfp4_gather(const void* packed, const void* scales, const int32_t* block_table,
+                     const int32_t* seq_lens, void* output, int32_t batch, int32_t max_tokens,
+                     int32_t table_width, int32_t n_heads, int32_t head_dim, int32_t page_size,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWZ_B200_H */

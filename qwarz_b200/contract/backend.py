@@ -1,0 +1,65 @@
+"""Split/combine ABI of libqwz_b200.so in the reference's argument order.
+
+Split (tests/test_attention_kernel_abi.py:16-20): 15 named arguments, then
+the two trailing pointer slots the reference's kernel wrapper appends
+(global_scratch, profile_scratch).  Arguments 11, 12, 13 are int32 (the
+indices a CUDA graph patches per replay in the reference, :25-31); combine
+argument 4 (num_splits) is int32.
+"""
+from __future__ import annotations
+
+from .. import _lib
+
+SPLIT_ARG_NAMES = (
+    "q", "k_cache", "v_cache", "block_table", "cache_seqlens", "out",
+    "partial_o", "partial_ml", "k_scales", "v_scales", "h32",
+    "split_len", "num_pages_per_seq", "num_splits", "sinks",
+)
+TRAILING_ARG_NAMES = ("global_scratch", "profile_scratch")
+INT32_ARG_INDEX = (11, 12, 13)
+COMBINE_ARG_NAMES = ("partial_o", "partial_ml", "out", "h32", "num_splits", "sinks")
+COMBINE_INT32_ARG_INDEX = (4,)
+
+# Launch policy of the sm_100a kernels (cf. the reference's
+# hybrid.DECODE_POLICY for its Triton Attention64 split kernel).
+DECODE_POLICY = {
+    "q1": {"kernel": "nvfp4_decode_kernel", "warps": 4, "stage_tokens": 64, "stages": 4,
+           "mma": "m16n8k16 tokens x heads(6->8)", "ctas_per_sm": 2},
+    "q2-8": {"kernel": "nvfp4_verify_kernel", "warps": 4, "stage_tokens": 64, "stages": 3,
+             "mma": "m16n8k16 tokens x rows(6*q_len->8*NT)", "ctas_per_sm": 2},
+    "draft": {"kernel": "fp8_decode_kernel", "warps": 4, "stage_tokens": 64, "stages": 3,
+              "splits": 16},
+    "combine": {"kernel": "lse_combine_kernel", "threads": 256, "split_groups": 8},
+}
+
+
+def pack_split_args(ptrs: dict, ints: dict) -> list[tuple[str, str, int]]:
+    """(name, kind, value) for the 15 + 2 split arguments in ABI order; kind
+    is "int32" at INT32_ARG_INDEX and "ptr" elsewhere (missing pointers = 0)."""
+    packed = []
+    for index, name in enumerate(SPLIT_ARG_NAMES + TRAILING_ARG_NAMES):
+        if index in INT32_ARG_INDEX:
+            value = int(ints[name])
+            if not -(1 << 31) <= value < (1 << 31):
+                raise ValueError(f"{name} does not fit int32: {value}")
+            packed.append((name, "int32", value))
+        else:
+            packed.append((name, "ptr", int(ptrs.get(name, 0) or 0)))
+    return packed
+
+
+def call_split(packed, q_len: int, num_pages: int, sm_scale: float, dtype: int, stream: int) -> None:
+    """Invoke qwz_attn_split with a `pack_split_args` list (stream: cudaStream_t as int)."""
+    if [n for n, _, _ in packed] != list(SPLIT_ARG_NAMES + TRAILING_ARG_NAMES):
+        raise ValueError("packed arguments are not in ABI order")
+    values = [v if k == "int32" else (v or None) for _, k, v in packed]
+    lib = _lib.load()
+    _lib.check(lib.qwz_attn_split(*values, q_len, num_pages, float(sm_scale), dtype, stream),
+               "qwz_attn_split")
+
+
+def call_combine(partial_o: int, partial_ml: int, out: int, num_splits: int, q_len: int,
+                 dtype: int, stream: int) -> None:
+    lib = _lib.load()
+    _lib.check(lib.qwz_attn_combine(partial_o, partial_ml, out, None, num_splits, None, q_len,
+                                    dtype, stream), "qwz_attn_combine")

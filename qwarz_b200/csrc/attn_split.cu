@@ -1,0 +1,980 @@
+// Split-K paged attention over the NVFP4 one-level KV cache (decode and MTP
+// verify) and over the FP8 shadow KV of the MTP draft, for sm_100a.
+//
+// Replaces, behind the reference's split/combine ABI
+// (tests/test_attention_kernel_abi.py:13-55), the FlashInfer XQA launch of
+// src/qwasar_runtime/xqa.py:484-554 (q_len <= 8 over NVFP4 pages) and the
+// Triton draft split-K of engine/forward/draft_attention.py:23-61.
+//
+// Work decomposition.  One CTA owns one KV head and one contiguous chunk of
+// 64-token stages.  Stages are staged global->shared with 16-byte cp.async
+// into a multi-buffer ring (XOR-swizzled rows, so every fragment load below
+// is bank-conflict free).  Dequantisation happens in registers straight into
+// mma.sync fragments: codes -> f16 with the hardware E2M1/E4M3 converts and
+// one f16x2 multiply by the block scale (exact: an E2M1 value times an E4M3
+// scale has at most 6 significant bits and lies inside the FP16 range).
+//
+// Decode (q_len = 1): tokens are the MMA M dimension and the 6 GQA heads
+// (padded to 8) the N dimension, so one warp holds the whole 256 x 8 output
+// tile of its head group in registers and never exchanges data with other
+// warps until the epilogue.  S^T comes out with tokens on rows; movmatrix
+// turns it into the P^T B-fragment of the PV product.  The head-dim
+// contraction of QK uses a permuted d order (k-step s of lane quad q covers
+// d = 64q + 4s + {0..3}) so every A fragment register is one code byte.
+//
+// Verify (q_len 2..8, 6*q_len rows): phase 1 splits the 64-token stage by
+// tokens (warp w: tokens 16w..16w+15, full head dim, Q from shared memory by
+// ldmatrix), phase 2 splits the head dim (warp w: d in [64w, 64w+64)) so the
+// 48 x 256 FP32 output tile fits in registers.  The column maxima and P
+// (FP16) cross phases through shared memory.
+//
+// Online softmax is base-2 with lazy rescaling: the reference maximum of a
+// column only moves when a tile exceeds it by more than 2^8, so p <= 256 and
+// the O rescale is rare.  Partials are (m, l, O) with O unnormalised and m in
+// log2 units of sm_scale * q.k.
+
+#include "qwz_common.cuh"
+#include "qwz_kernels.h"
+
+#include <math_constants.h>
+
+namespace qwz {
+
+namespace {
+
+constexpr float kLazy = 8.0f;
+constexpr unsigned kFull = 0xffffffffu;
+
+QWZ_DEVINL float shfl_xor(float v, int m) { return __shfl_xor_sync(kFull, v, m); }
+
+// Four E4M3 scale bytes -> four broadcast f16x2 (s_i, s_i).
+QWZ_DEVINL void scales_bcast4(uint32_t ks, uint32_t (&sc)[4]) {
+  uint32_t h01, h23;
+  e4m3x4_to_f16x2x2(ks, h01, h23);
+  sc[0] = __byte_perm(h01, 0, 0x1010);
+  sc[1] = __byte_perm(h01, 0, 0x3232);
+  sc[2] = __byte_perm(h23, 0, 0x1010);
+  sc[3] = __byte_perm(h23, 0, 0x3232);
+}
+
+// Power-of-two factor that brings a row amax into [2^14, 2^15), so a BF16
+// (or FP16) query row converts to FP16 without overflow and, apart from
+// elements below amax * 2^-24, exactly.  Returns the factor.
+QWZ_DEVINL float pow2_row_scale(float amax) {
+  int e = 0;
+  if (amax > 0.f && amax < CUDART_INF_F) frexpf(amax, &e);
+  int k = 15 - e;
+  k = k > 120 ? 120 : (k < -120 ? -120 : k);
+  return ldexpf(1.0f, k);
+}
+
+// Decode-layout Q fragments.  Lane (g, q) holds row g of the head group,
+// d in [64q, 64q+64) as 32 f16x2 words; rows 6,7 are zero padding.
+template <typename T>
+QWZ_DEVINL void load_q_decode(const T* q, int row, int qd, float sm_scale_log2,
+                              uint32_t (&qf)[32], float& cf0, float& cf1) {
+  if (row >= 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)row * kHeadDim + 64 * qd);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 v = __ldg(src + i);
+      qf[4 * i + 0] = v.x;
+      qf[4 * i + 1] = v.y;
+      qf[4 * i + 2] = v.z;
+      qf[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qf[i] = 0u;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float2 f = InTraits<T>::to_float2(qf[i]);
+    amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  amax = fmaxf(amax, shfl_xor(amax, 1));
+  amax = fmaxf(amax, shfl_xor(amax, 2));
+  const float sc = pow2_row_scale(amax);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float2 f = InTraits<T>::to_float2(qf[i]);
+    qf[i] = pack_half2(f.x * sc, f.y * sc);
+  }
+  const float rowfac = sm_scale_log2 / sc;
+  const int lane = threadIdx.x & 31;
+  (void)lane;
+  cf0 = __shfl_sync(kFull, rowfac, 4 * (2 * qd));
+  cf1 = __shfl_sync(kFull, rowfac, 4 * (2 * qd + 1));
+}
+
+// Token range of this split, in stages of ST tokens.
+struct StageRange {
+  int tok_end;  // exclusive end of the valid tokens (post-append length clipped)
+  int st_lo;
+  int n_st;
+};
+
+template <int ST>
+QWZ_DEVINL StageRange stage_range(const SplitParams& p, int split) {
+  StageRange r;
+  const int L = __ldg(p.seqlens) + p.len_add;
+  const long long end = (long long)p.tok_begin + (long long)p.tok_span;
+  r.tok_end = (int)min((long long)L, end);
+  const int n_tok = max(r.tok_end - p.tok_begin, 0);
+  const int total = (n_tok + ST - 1) / ST;
+  int lo, hi;
+  if (p.split_len > 0) {
+    const int per = p.split_len / ST;
+    lo = split * per;
+    hi = min(lo + per, total);
+  } else {
+    lo = (int)(((long long)split * total) / p.num_splits);
+    hi = (int)(((long long)(split + 1) * total) / p.num_splits);
+  }
+  r.st_lo = lo;
+  r.n_st = max(hi - lo, 0);
+  return r;
+}
+
+// Physical page of the 256-token page holding logical token t, or -1.
+QWZ_DEVINL int lookup_page(const SplitParams& p, int t, bool report) {
+  const int lp = (t >> 8) - p.table_page_offset;
+  if (lp < 0 || lp >= p.table_width) {
+    if (report) flag_error(kErrTableRange);
+    return -1;
+  }
+  const int pp = __ldg(p.block_table + lp);
+  if (pp < 0 || pp >= p.num_pages) {
+    if (report) flag_error(kErrPageRange);
+    return -1;
+  }
+  return pp;
+}
+
+// One online-softmax step on a 16-token x 8-column S^T fragment.
+// s: raw scores (c-fragment), returns the two P^T B-fragment registers.
+QWZ_DEVINL void softmax_step_decode(float (&t)[4], float& m0, float& m1, float& l0,
+                                    float& l1, float (&o)[16][4], uint32_t& pb0,
+                                    uint32_t& pb1) {
+  float mx0 = fmaxf(t[0], t[2]);
+  float mx1 = fmaxf(t[1], t[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, shfl_xor(mx0, off));
+    mx1 = fmaxf(mx1, shfl_xor(mx1, off));
+  }
+  const bool need = (mx0 > m0 + kLazy) || (mx1 > m1 + kLazy);
+  if (__any_sync(kFull, need)) {
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float a0 = (n0 == -CUDART_INF_F) ? 1.f : exp2_approx(m0 - n0);
+    const float a1 = (n1 == -CUDART_INF_F) ? 1.f : exp2_approx(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    l0 *= a0;
+    l1 *= a1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      o[j][0] *= a0;
+      o[j][1] *= a1;
+      o[j][2] *= a0;
+      o[j][3] *= a1;
+    }
+  }
+  const float mu0 = (m0 == -CUDART_INF_F) ? 0.f : m0;
+  const float mu1 = (m1 == -CUDART_INF_F) ? 0.f : m1;
+  const float p0 = exp2_approx(t[0] - mu0), p1 = exp2_approx(t[1] - mu1);
+  const float p2 = exp2_approx(t[2] - mu0), p3 = exp2_approx(t[3] - mu1);
+  l0 += p0 + p2;
+  l1 += p1 + p3;
+  t[0] = p0;
+  t[1] = p1;
+  t[2] = p2;
+  t[3] = p3;
+  pb0 = movmatrix_trans(pack_half2(p0, p1));
+  pb1 = movmatrix_trans(pack_half2(p2, p3));
+}
+
+// Cross-warp merge of decode-layout (m, l, O) and the partial store.
+// dmap(g, j) gives the head-dim index of accumulator row g of m-tile j.
+template <int WARPS, class DMap>
+QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, int kvh,
+                                float m0, float m1, float l0, float l1,
+                                const float (&o)[16][4], DMap dmap) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += shfl_xor(l0, off);
+    l1 += shfl_xor(l1, off);
+  }
+  float* red = reinterpret_cast<float*>(smem);          // [WARPS][8][256]
+  float* mlred = red + WARPS * 8 * kHeadDim;              // [WARPS][8][2]
+  float* ow = red + warp * 8 * kHeadDim;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = dmap(g, j);
+    *reinterpret_cast<float2*>(ow + (2 * qd) * kHeadDim + d) = make_float2(o[j][0], o[j][2]);
+    *reinterpret_cast<float2*>(ow + (2 * qd + 1) * kHeadDim + d) = make_float2(o[j][1], o[j][3]);
+  }
+  if (g == 0) {
+    mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
+    mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < kGroup * kHeadDim; idx += WARPS * 32) {
+    const int col = idx >> 8, d = idx & 255;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, mlred[(w * 8 + col) * 2]);
+    float acc = 0.f, ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      const float mw = mlred[(w * 8 + col) * 2];
+      const float wt = (mw == -CUDART_INF_F) ? 0.f : exp2_approx(mw - M);
+      acc += wt * red[(w * 8 + col) * kHeadDim + d];
+      ls += wt * mlred[(w * 8 + col) * 2 + 1];
+    }
+    const size_t R = (size_t)(kvh * kGroup + col);
+    const size_t base = R * p.num_splits + split;
+    p.partial_o[base * kHeadDim + d] = acc;
+    if (d == 0) {
+      p.partial_ml[base * 2 + 0] = M;
+      p.partial_ml[base * 2 + 1] = ls;
+    }
+  }
+}
+
+}  // namespace
+
+// =====================================================================
+// NVFP4 decode, q_len = 1.
+// =====================================================================
+template <typename T, int WARPS, int NST>
+__global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const SplitParams p) {
+  constexpr int ST = WARPS * 16;
+  constexpr int CODE_TILE = ST * kCodeBytes;
+  constexpr int SCALE_TILE = ST * kScaleBytes;
+  constexpr int STAGE_BYTES = 2 * CODE_TILE + 2 * SCALE_TILE;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+
+  const StageRange rg = stage_range<ST>(p, split);
+
+  uint32_t qf[32];
+  float cf0, cf1;
+  load_q_decode<T>(reinterpret_cast<const T*>(p.q), g < kGroup ? kvh * kGroup + g : -1, qd,
+                   p.sm_scale_log2, qf, cf0, cf1);
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+
+  const uint8_t* kc = p.k_codes;
+  const uint8_t* vc = p.v_codes;
+  const uint8_t* ks = p.k_scales;
+  const uint8_t* vs = p.v_scales;
+
+  auto issue = [&](int k) {
+    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+    const int pp = lookup_page(p, t0, tid == 0);
+    const size_t rowbase = (size_t)(pp < 0 ? 0 : pp) * kPage + (t0 & (kPage - 1));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + (i & 3) * (2 * ST);
+      const int row = idx >> 3, ch = idx & 7;
+      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
+      const uint8_t* base = (i < 4) ? kc : vc;
+      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kCodeBytes + ch * 16 : base;
+      cp_async16(slot + (i >> 2) * CODE_TILE + swz128(row, ch), src, ok ? 16u : 0u);
+    }
+    {
+      const int tensor = tid >= ST ? 1 : 0;
+      const int row = tid - tensor * ST;
+      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
+      const uint8_t* base = tensor ? vs : ks;
+      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kScaleBytes : base;
+      cp_async16(slot + 2 * CODE_TILE + tensor * SCALE_TILE + row * 16, src, ok ? 16u : 0u);
+    }
+  };
+
+#pragma unroll
+  for (int k = 0; k < NST - 1; ++k) {
+    if (k < rg.n_st) issue(k);
+    cp_async_commit();
+  }
+
+  for (int k = 0; k < rg.n_st; ++k) {
+    cp_async_wait<NST - 2>();
+    __syncthreads();
+    if (k + NST - 1 < rg.n_st) issue(k + NST - 1);
+    cp_async_commit();
+
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+    const int tw0 = p.tok_begin + (rg.st_lo + k) * ST + 16 * warp;
+
+    // ---------------- S^T = K Q^T over the 16 tokens of this warp
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    uint32_t kw0[8], kw1[8];
+    {
+      const uint4 a = lds128(slot + swz128(r0, 2 * qd));
+      const uint4 b = lds128(slot + swz128(r0, 2 * qd + 1));
+      const uint4 c = lds128(slot + swz128(r1, 2 * qd));
+      const uint4 d = lds128(slot + swz128(r1, 2 * qd + 1));
+      kw0[0] = a.x; kw0[1] = a.y; kw0[2] = a.z; kw0[3] = a.w;
+      kw0[4] = b.x; kw0[5] = b.y; kw0[6] = b.z; kw0[7] = b.w;
+      kw1[0] = c.x; kw1[1] = c.y; kw1[2] = c.z; kw1[3] = c.w;
+      kw1[4] = d.x; kw1[5] = d.y; kw1[6] = d.z; kw1[7] = d.w;
+    }
+    uint32_t sc0[4], sc1[4];
+    scales_bcast4(lds32(slot + 2 * CODE_TILE + r0 * 16 + 4 * qd), sc0);
+    scales_bcast4(lds32(slot + 2 * CODE_TILE + r1 * 16 + 4 * qd), sc1);
+
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) {
+      uint32_t h0[4], h1[4];
+      e2m1x8_to_f16x2x4(kw0[w8], h0);
+      e2m1x8_to_f16x2x4(kw1[w8], h1);
+      const uint32_t s0 = sc0[w8 >> 1], s1 = sc1[w8 >> 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        h0[j] = hmul2_u32(h0[j], s0);
+        h1[j] = hmul2_u32(h1[j], s1);
+      }
+      mma_16816(sa, h0[0], h1[0], h0[1], h1[1], qf[4 * w8 + 0], qf[4 * w8 + 1]);
+      mma_16816(sb, h0[2], h1[2], h0[3], h1[3], qf[4 * w8 + 2], qf[4 * w8 + 3]);
+    }
+    float t[4] = {(sa[0] + sb[0]) * cf0, (sa[1] + sb[1]) * cf1, (sa[2] + sb[2]) * cf0,
+                  (sa[3] + sb[3]) * cf1};
+    if (tw0 + 16 > rg.tok_end) {
+      if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
+      if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
+    }
+    uint32_t pb0, pb1;
+    softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
+
+    // ---------------- O^T += V^T P^T
+    const int ra = 16 * warp + 2 * qd;
+    const uint32_t vbase = slot + CODE_TILE;
+    const uint4 va = lds128(vbase + swz128(ra, g));
+    const uint4 vb = lds128(vbase + swz128(ra + 1, g));
+    const uint4 vcc = lds128(vbase + swz128(ra + 8, g));
+    const uint4 vd = lds128(vbase + swz128(ra + 9, g));
+    const uint32_t vsb = slot + 2 * CODE_TILE + SCALE_TILE + 2 * g;
+    const uint32_t sa16 = lds16(vsb + ra * 16), sb16 = lds16(vsb + (ra + 1) * 16);
+    const uint32_t sc16 = lds16(vsb + (ra + 8) * 16), sd16 = lds16(vsb + (ra + 9) * 16);
+    uint32_t spab0, spab1, spcd0, spcd1;
+    e4m3x4_to_f16x2x2(__byte_perm(sa16, sb16, 0x5140), spab0, spab1);
+    e4m3x4_to_f16x2x2(__byte_perm(sc16, sd16, 0x5140), spcd0, spcd1);
+    const uint32_t VA[4] = {va.x, va.y, va.z, va.w};
+    const uint32_t VB[4] = {vb.x, vb.y, vb.z, vb.w};
+    const uint32_t VC[4] = {vcc.x, vcc.y, vcc.z, vcc.w};
+    const uint32_t VD[4] = {vd.x, vd.y, vd.z, vd.w};
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) {
+      const uint32_t xab = (VA[w4] & 0x0F0F0F0Fu) | ((VB[w4] << 4) & 0xF0F0F0F0u);
+      const uint32_t yab = ((VA[w4] >> 4) & 0x0F0F0F0Fu) | (VB[w4] & 0xF0F0F0F0u);
+      const uint32_t xcd = (VC[w4] & 0x0F0F0F0Fu) | ((VD[w4] << 4) & 0xF0F0F0F0u);
+      const uint32_t ycd = ((VC[w4] >> 4) & 0x0F0F0F0Fu) | (VD[w4] & 0xF0F0F0F0u);
+      uint32_t hxab[4], hyab[4], hxcd[4], hycd[4];
+      e2m1x8_to_f16x2x4(xab, hxab);
+      e2m1x8_to_f16x2x4(yab, hyab);
+      e2m1x8_to_f16x2x4(xcd, hxcd);
+      e2m1x8_to_f16x2x4(ycd, hycd);
+      const uint32_t sab = w4 < 2 ? spab0 : spab1;
+      const uint32_t scd = w4 < 2 ? spcd0 : spcd1;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        mma_16816(o[4 * w4 + kk], hmul2_u32(hxab[kk], sab), hmul2_u32(hyab[kk], sab),
+                  hmul2_u32(hxcd[kk], scd), hmul2_u32(hycd[kk], scd), pb0, pb1);
+      }
+    }
+  }
+
+  cp_async_wait<0>();
+  __syncthreads();
+  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o,
+                         [](int gg, int j) { return 32 * gg + 2 * j; });
+}
+
+// =====================================================================
+// NVFP4 verify, q_len 2..8 (rows = 6 * q_len <= 8 * NT).
+// =====================================================================
+template <typename T, int NT, int NST>
+__global__ void __launch_bounds__(128, 2) nvfp4_verify_kernel(const SplitParams p) {
+  constexpr int WARPS = 4, ST = 64;
+  constexpr int CODE_TILE = ST * kCodeBytes;
+  constexpr int SCALE_TILE = ST * kScaleBytes;
+  constexpr int STAGE_BYTES = 2 * CODE_TILE + 2 * SCALE_TILE;
+  constexpr int NCOL = 8 * NT;
+  constexpr int Q_OFF = NST * STAGE_BYTES;
+  constexpr int P_OFF = Q_OFF + NCOL * 512;
+  constexpr int P_BYTES = NCOL * 128;
+  constexpr int CM_OFF = P_OFF + 2 * P_BYTES;
+  constexpr int CF_OFF = CM_OFF + 2 * WARPS * NCOL * 4;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int ncol_real = p.q_len * kGroup;
+
+  const StageRange rg = stage_range<ST>(p, split);
+  const int L_pre = __ldg(p.seqlens) + p.len_add - p.q_len;
+
+  float* colmax = reinterpret_cast<float*>(smem + CM_OFF);  // [2][WARPS][NCOL]
+  float* colfac = reinterpret_cast<float*>(smem + CF_OFF);  // [NCOL]
+
+  // ---------------- Q -> shared (FP16, permuted d order, swizzled rows)
+  {
+    const T* q = reinterpret_cast<const T*>(p.q);
+    for (int c = warp; c < NCOL; c += WARPS) {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+      if (c < ncol_real) {
+        const int qi = c / kGroup, hg = c - qi * kGroup;
+        const int row = qi * kQHeads + kvh * kGroup + hg;
+        raw = __ldg(reinterpret_cast<const uint4*>(q + (size_t)row * kHeadDim) + lane);
+      }
+      const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = InTraits<T>::to_float2(rw[i]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) amax = fmaxf(amax, shfl_xor(amax, off));
+      const float sc = pow2_row_scale(amax);
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = InTraits<T>::to_float2(rw[i]);
+        h[i] = pack_half2(f.x * sc, f.y * sc);
+      }
+      // lane holds d = 8*lane .. 8*lane+7: quad q = lane/8, k-steps s0, s0+1.
+      const int qq = lane >> 3, s0 = 2 * (lane & 7);
+#pragma unroll
+      for (int hs = 0; hs < 2; ++hs) {
+        const int s = s0 + hs;
+        // d = 64q + 4s + {0,1} -> logical k {2q, 2q+1} (chunk 2s);
+        // d = 64q + 4s + {2,3} -> logical k {2q+8, 2q+9} (chunk 2s+1).
+        const uint32_t rowb = sbase + Q_OFF + c * 512;
+        sts32(rowb + (((2 * s) ^ (c & 7)) << 4) + 4 * qq, h[2 * hs]);
+        sts32(rowb + (((2 * s + 1) ^ (c & 7)) << 4) + 4 * qq, h[2 * hs + 1]);
+      }
+      if (lane == 0) colfac[c] = (c < ncol_real) ? p.sm_scale_log2 / sc : 0.f;
+    }
+  }
+
+  float o[4][NT][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[j][n][0] = o[j][n][1] = o[j][n][2] = o[j][n][3] = 0.f;
+  float mref[NT][2], lpart[NT][2];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    mref[n][0] = mref[n][1] = -CUDART_INF_F;
+    lpart[n][0] = lpart[n][1] = 0.f;
+  }
+
+  auto issue = [&](int k) {
+    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+    const int pp = lookup_page(p, t0, tid == 0);
+    const size_t rowbase = (size_t)(pp < 0 ? 0 : pp) * kPage + (t0 & (kPage - 1));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + (i & 3) * (2 * ST);
+      const int row = idx >> 3, ch = idx & 7;
+      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
+      const uint8_t* base = (i < 4) ? p.k_codes : p.v_codes;
+      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kCodeBytes + ch * 16 : base;
+      cp_async16(slot + (i >> 2) * CODE_TILE + swz128(row, ch), src, ok ? 16u : 0u);
+    }
+    {
+      const int tensor = tid >= ST ? 1 : 0;
+      const int row = tid - tensor * ST;
+      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
+      const uint8_t* base = tensor ? p.v_scales : p.k_scales;
+      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kScaleBytes : base;
+      cp_async16(slot + 2 * CODE_TILE + tensor * SCALE_TILE + row * 16, src, ok ? 16u : 0u);
+    }
+  };
+
+#pragma unroll
+  for (int k = 0; k < NST - 1; ++k) {
+    if (k < rg.n_st) issue(k);
+    cp_async_commit();
+  }
+
+  for (int k = 0; k < rg.n_st; ++k) {
+    cp_async_wait<NST - 2>();
+    __syncthreads();
+    if (k + NST - 1 < rg.n_st) issue(k + NST - 1);
+    cp_async_commit();
+
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+    const int buf = k & 1;
+    const int tw0 = p.tok_begin + (rg.st_lo + k) * ST + 16 * warp;
+
+    // ---------------- phase 1: S^T for tokens 16w..16w+15, all columns
+    float s[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    {
+      const int r0 = 16 * warp + g, r1 = r0 + 8;
+      uint32_t kw0[8], kw1[8];
+      const uint4 a = lds128(slot + swz128(r0, 2 * qd));
+      const uint4 b = lds128(slot + swz128(r0, 2 * qd + 1));
+      const uint4 c = lds128(slot + swz128(r1, 2 * qd));
+      const uint4 d = lds128(slot + swz128(r1, 2 * qd + 1));
+      kw0[0] = a.x; kw0[1] = a.y; kw0[2] = a.z; kw0[3] = a.w;
+      kw0[4] = b.x; kw0[5] = b.y; kw0[6] = b.z; kw0[7] = b.w;
+      kw1[0] = c.x; kw1[1] = c.y; kw1[2] = c.z; kw1[3] = c.w;
+      kw1[4] = d.x; kw1[5] = d.y; kw1[6] = d.z; kw1[7] = d.w;
+      uint32_t sc0[4], sc1[4];
+      scales_bcast4(lds32(slot + 2 * CODE_TILE + r0 * 16 + 4 * qd), sc0);
+      scales_bcast4(lds32(slot + 2 * CODE_TILE + r1 * 16 + 4 * qd), sc1);
+      const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) {
+        uint32_t h0[4], h1[4];
+        e2m1x8_to_f16x2x4(kw0[w8], h0);
+        e2m1x8_to_f16x2x4(kw1[w8], h1);
+        const uint32_t s0 = sc0[w8 >> 1], s1 = sc1[w8 >> 1];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          h0[j] = hmul2_u32(h0[j], s0);
+          h1[j] = hmul2_u32(h1[j], s1);
+        }
+#pragma unroll
+        for (int hs = 0; hs < 2; ++hs) {
+          const int ks = 2 * w8 + hs;
+#pragma unroll
+          for (int np = 0; np < NT / 2; ++np) {
+            const int cc = 8 * (2 * np + (mi >> 1)) + ri;
+            const int chunk = 2 * ks + (mi & 1);
+            uint32_t b00, b01, b10, b11;
+            ldmatrix_x4(b00, b01, b10, b11, sbase + Q_OFF + cc * 512 + ((chunk ^ ri) << 4));
+            mma_16816(s[2 * np], h0[2 * hs], h1[2 * hs], h0[2 * hs + 1], h1[2 * hs + 1], b00, b01);
+            mma_16816(s[2 * np + 1], h0[2 * hs], h1[2 * hs], h0[2 * hs + 1], h1[2 * hs + 1], b10, b11);
+          }
+          if (NT & 1) {
+            const int cc = 8 * (NT - 1) + ri;
+            const int chunk = 2 * ks + (mi & 1);
+            uint32_t b0, b1;
+            ldmatrix_x2(b0, b1, sbase + Q_OFF + cc * 512 + ((chunk ^ ri) << 4));
+            mma_16816(s[NT - 1], h0[2 * hs], h1[2 * hs], h0[2 * hs + 1], h1[2 * hs + 1], b0, b1);
+          }
+        }
+      }
+    }
+
+    // scale, mask (causal inside the window, end of sequence), column max
+    const bool tail = (tw0 + 15 > L_pre) || (tw0 + 16 > rg.tok_end);
+    float cm[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int c0 = 8 * n + 2 * qd;
+      const float2 f = *reinterpret_cast<const float2*>(colfac + c0);
+      s[n][0] *= f.x;
+      s[n][1] *= f.y;
+      s[n][2] *= f.x;
+      s[n][3] *= f.y;
+      if (tail) {
+        const int ta = tw0 + g, tb = ta + 8;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int c = c0 + jj;
+          if (c < ncol_real) {
+            const int lim = L_pre + c / kGroup;  // last visible token (inclusive)
+            if (ta > lim || ta >= rg.tok_end) s[n][jj] = -CUDART_INF_F;
+            if (tb > lim || tb >= rg.tok_end) s[n][2 + jj] = -CUDART_INF_F;
+          }
+        }
+      }
+      cm[n][0] = fmaxf(s[n][0], s[n][2]);
+      cm[n][1] = fmaxf(s[n][1], s[n][3]);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        cm[n][0] = fmaxf(cm[n][0], shfl_xor(cm[n][0], off));
+        cm[n][1] = fmaxf(cm[n][1], shfl_xor(cm[n][1], off));
+      }
+    }
+    float* cmw = colmax + (buf * WARPS + warp) * NCOL;
+    if (g == 0) {
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+        *reinterpret_cast<float2*>(cmw + 8 * n + 2 * qd) = make_float2(cm[n][0], cm[n][1]);
+    }
+    __syncthreads();
+    bool need = false;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int c = 8 * n + 2 * qd + jj;
+        float tm = colmax[(buf * WARPS + 0) * NCOL + c];
+#pragma unroll
+        for (int w = 1; w < WARPS; ++w) tm = fmaxf(tm, colmax[(buf * WARPS + w) * NCOL + c]);
+        cm[n][jj] = tm;
+        need |= tm > mref[n][jj] + kLazy;
+      }
+    }
+    const bool rescale = __any_sync(kFull, need);
+    float alpha[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        alpha[n][jj] = 1.f;
+        if (rescale) {
+          const float nm = fmaxf(mref[n][jj], cm[n][jj]);
+          alpha[n][jj] = (nm == -CUDART_INF_F) ? 1.f : exp2_approx(mref[n][jj] - nm);
+          mref[n][jj] = nm;
+          lpart[n][jj] *= alpha[n][jj];
+        }
+      }
+    }
+    const uint32_t pbuf = sbase + P_OFF + buf * P_BYTES;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const float mu0 = (mref[n][0] == -CUDART_INF_F) ? 0.f : mref[n][0];
+      const float mu1 = (mref[n][1] == -CUDART_INF_F) ? 0.f : mref[n][1];
+      const float p0 = exp2_approx(s[n][0] - mu0), p1 = exp2_approx(s[n][1] - mu1);
+      const float p2 = exp2_approx(s[n][2] - mu0), p3 = exp2_approx(s[n][3] - mu1);
+      lpart[n][0] += p0 + p2;
+      lpart[n][1] += p1 + p3;
+      const uint32_t u0 = movmatrix_trans(pack_half2(p0, p1));
+      const uint32_t u1 = movmatrix_trans(pack_half2(p2, p3));
+      const int col = 8 * n + g;
+      const int tl0 = 16 * warp + 2 * qd;  // token (local to the stage) of u0; u1 is +8
+      sts32(pbuf + col * 128 + ((((tl0 >> 3)) ^ (col & 7)) << 4) + (tl0 & 7) * 2, u0);
+      sts32(pbuf + col * 128 + ((((tl0 + 8) >> 3) ^ (col & 7)) << 4) + (tl0 & 7) * 2, u1);
+    }
+    __syncthreads();
+
+    // ---------------- phase 2: O^T[d in 64w..64w+63] += V^T P^T
+    if (rescale) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          o[j][n][0] *= alpha[n][0];
+          o[j][n][1] *= alpha[n][1];
+          o[j][n][2] *= alpha[n][0];
+          o[j][n][3] *= alpha[n][1];
+        }
+    }
+    const uint32_t vbase = slot + CODE_TILE;
+    const uint32_t vsb = slot + 2 * CODE_TILE + SCALE_TILE + 4 * warp + (g >> 1);
+    const int vchunk = 2 * warp + (g >> 2);
+    const int vword = (g & 3) * 4;
+    const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int ta = 16 * kk + 2 * qd;
+      const uint32_t Wa = lds32(vbase + ta * 128 + ((vchunk ^ (ta & 7)) << 4) + vword);
+      const uint32_t Wb = lds32(vbase + (ta + 1) * 128 + ((vchunk ^ ((ta + 1) & 7)) << 4) + vword);
+      const uint32_t Wc = lds32(vbase + (ta + 8) * 128 + ((vchunk ^ ((ta + 8) & 7)) << 4) + vword);
+      const uint32_t Wd = lds32(vbase + (ta + 9) * 128 + ((vchunk ^ ((ta + 9) & 7)) << 4) + vword);
+      const uint32_t sa8 = lds8(vsb + ta * 16), sb8 = lds8(vsb + (ta + 1) * 16);
+      const uint32_t sc8 = lds8(vsb + (ta + 8) * 16), sd8 = lds8(vsb + (ta + 9) * 16);
+      uint32_t spab, spcd, unused;
+      e4m3x4_to_f16x2x2(sa8 | (sb8 << 8), spab, unused);
+      e4m3x4_to_f16x2x2(sc8 | (sd8 << 8), spcd, unused);
+      const uint32_t xab = (Wa & 0x0F0F0F0Fu) | ((Wb << 4) & 0xF0F0F0F0u);
+      const uint32_t yab = ((Wa >> 4) & 0x0F0F0F0Fu) | (Wb & 0xF0F0F0F0u);
+      const uint32_t xcd = (Wc & 0x0F0F0F0Fu) | ((Wd << 4) & 0xF0F0F0F0u);
+      const uint32_t ycd = ((Wc >> 4) & 0x0F0F0F0Fu) | (Wd & 0xF0F0F0F0u);
+      uint32_t hxab[4], hyab[4], hxcd[4], hycd[4];
+      e2m1x8_to_f16x2x4(xab, hxab);
+      e2m1x8_to_f16x2x4(yab, hyab);
+      e2m1x8_to_f16x2x4(xcd, hxcd);
+      e2m1x8_to_f16x2x4(ycd, hycd);
+      uint32_t bfr[NT][2];
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        const int cc = 8 * (2 * np + (mi >> 1)) + ri;
+        const int chunk = 2 * kk + (mi & 1);
+        ldmatrix_x4(bfr[2 * np][0], bfr[2 * np][1], bfr[2 * np + 1][0], bfr[2 * np + 1][1],
+                    pbuf + cc * 128 + ((chunk ^ (cc & 7)) << 4));
+      }
+      if (NT & 1) {
+        const int cc = 8 * (NT - 1) + ri;
+        const int chunk = 2 * kk + (mi & 1);
+        ldmatrix_x2(bfr[NT - 1][0], bfr[NT - 1][1], pbuf + cc * 128 + ((chunk ^ (cc & 7)) << 4));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t a0 = hmul2_u32(hxab[j], spab), a1 = hmul2_u32(hyab[j], spab);
+        const uint32_t a2 = hmul2_u32(hxcd[j], spcd), a3 = hmul2_u32(hycd[j], spcd);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) mma_16816(o[j][n], a0, a1, a2, a3, bfr[n][0], bfr[n][1]);
+      }
+    }
+  }
+
+  cp_async_wait<0>();
+  __syncthreads();
+  // l: reduce over the 8 row-lanes, then over warps (token split of phase 1).
+  float* lred = colmax;  // [WARPS][NCOL]
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      float v = lpart[n][jj];
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) v += shfl_xor(v, off);
+      lpart[n][jj] = v;
+    }
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+      *reinterpret_cast<float2*>(lred + warp * NCOL + 8 * n + 2 * qd) =
+          make_float2(lpart[n][0], lpart[n][1]);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int c = 8 * n + 2 * qd + jj;
+      if (c >= ncol_real) continue;
+      const int qi = c / kGroup, hg = c - qi * kGroup;
+      const size_t R = (size_t)qi * kQHeads + kvh * kGroup + hg;
+      const size_t base = R * p.num_splits + split;
+      float* dst = p.partial_o + base * kHeadDim + 64 * warp + 8 * g;
+      *reinterpret_cast<float4*>(dst) =
+          make_float4(o[0][n][jj], o[0][n][2 + jj], o[1][n][jj], o[1][n][2 + jj]);
+      *reinterpret_cast<float4*>(dst + 4) =
+          make_float4(o[2][n][jj], o[2][n][2 + jj], o[3][n][jj], o[3][n][2 + jj]);
+      if (warp == 0 && g == 0) {
+        float ls = 0.f;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) ls += lred[w * NCOL + c];
+        p.partial_ml[base * 2 + 0] = mref[n][jj];
+        p.partial_ml[base * 2 + 1] = ls;
+      }
+    }
+  }
+}
+
+// =====================================================================
+// FP8 (E4M3) draft decode, q_len = 1, contiguous [T, 4, 256] K/V with an
+// optional FP32 scale per (256-token page, KV head).
+// =====================================================================
+QWZ_DEVINL uint32_t swz256(int row, int ch) {
+  return static_cast<uint32_t>(row * 256 + ((ch ^ (row & 7) ^ ((ch >> 3) << 1)) << 4));
+}
+
+template <int WARPS, int NST>
+__global__ void __launch_bounds__(WARPS * 32, 1) fp8_decode_kernel(const SplitParams p) {
+  constexpr int ST = WARPS * 16;
+  constexpr int TILE = ST * kHeadDim;  // one tensor, one head, ST tokens
+  constexpr int STAGE_BYTES = 2 * TILE;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+
+  const StageRange rg = stage_range<ST>(p, split);
+
+  uint32_t qf[32];
+  float cf0, cf1;
+  load_q_decode<__half>(reinterpret_cast<const __half*>(p.q),
+                        g < kGroup ? kvh * kGroup + g : -1, qd, p.sm_scale_log2, qf, cf0, cf1);
+
+  float o[16][4];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+
+  auto issue = [&](int k) {
+    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int idx = tid + (i & 7) * (WARPS * 32);
+      const int row = idx >> 4, ch = idx & 15;
+      const int t = t0 + row;
+      const bool ok = t < rg.tok_end && t < p.capacity;
+      const uint8_t* base = (i < 8) ? p.k_codes : p.v_codes;
+      const uint8_t* src = ok ? base + ((size_t)t * kKvHeads + kvh) * kHeadDim + ch * 16 : base;
+      cp_async16(slot + (i >> 3) * TILE + swz256(row, ch), src, ok ? 16u : 0u);
+    }
+  };
+
+#pragma unroll
+  for (int k = 0; k < NST - 1; ++k) {
+    if (k < rg.n_st) issue(k);
+    cp_async_commit();
+  }
+
+  for (int k = 0; k < rg.n_st; ++k) {
+    cp_async_wait<NST - 2>();
+    __syncthreads();
+    if (k + NST - 1 < rg.n_st) issue(k + NST - 1);
+    cp_async_commit();
+
+    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
+    const int tw0 = p.tok_begin + (rg.st_lo + k) * ST + 16 * warp;
+    const int page = tw0 >> 8;
+    const float kscale = p.k_page_scale ? __ldg(p.k_page_scale + page * kKvHeads + kvh) : 1.f;
+    const float vscale = p.v_page_scale ? __ldg(p.v_page_scale + page * kKvHeads + kvh) : 1.f;
+
+    const int r0 = 16 * warp + g, r1 = r0 + 8;
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      const uint4 a = lds128(slot + swz256(r0, 4 * qd + c4));
+      const uint4 b = lds128(slot + swz256(r1, 4 * qd + c4));
+      const uint32_t A[4] = {a.x, a.y, a.z, a.w};
+      const uint32_t B[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const int ks = 4 * c4 + w;
+        uint32_t a0, a2, a1, a3;
+        e4m3x4_to_f16x2x2(A[w], a0, a2);
+        e4m3x4_to_f16x2x2(B[w], a1, a3);
+        if (w & 1)
+          mma_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+        else
+          mma_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+      }
+    }
+    const float f0 = cf0 * kscale, f1 = cf1 * kscale;
+    float t[4] = {(sa[0] + sb[0]) * f0, (sa[1] + sb[1]) * f1, (sa[2] + sb[2]) * f0,
+                  (sa[3] + sb[3]) * f1};
+    if (tw0 + 16 > rg.tok_end) {
+      if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
+      if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
+    }
+    uint32_t pb0, pb1;
+    if (vscale == 1.f) {
+      softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
+    } else {
+      softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
+      pb0 = movmatrix_trans(pack_half2(t[0] * vscale, t[1] * vscale));
+      pb1 = movmatrix_trans(pack_half2(t[2] * vscale, t[3] * vscale));
+    }
+
+    const int ra = 16 * warp + 2 * qd;
+    const uint32_t vbase = slot + TILE;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int ch = g + 8 * half;
+      const uint4 va = lds128(vbase + swz256(ra, ch));
+      const uint4 vb = lds128(vbase + swz256(ra + 1, ch));
+      const uint4 vcc = lds128(vbase + swz256(ra + 8, ch));
+      const uint4 vd = lds128(vbase + swz256(ra + 9, ch));
+      const uint32_t VA[4] = {va.x, va.y, va.z, va.w};
+      const uint32_t VB[4] = {vb.x, vb.y, vb.z, vb.w};
+      const uint32_t VC[4] = {vcc.x, vcc.y, vcc.z, vcc.w};
+      const uint32_t VD[4] = {vd.x, vd.y, vd.z, vd.w};
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const uint32_t sel = pr ? 0x7362u : 0x5140u;
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2x2(__byte_perm(VA[w], VB[w], sel), a0, a1);
+          e4m3x4_to_f16x2x2(__byte_perm(VC[w], VD[w], sel), a2, a3);
+          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pb0, pb1);
+        }
+      }
+    }
+  }
+
+  cp_async_wait<0>();
+  __syncthreads();
+  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int gg, int j) {
+    return j < 8 ? 16 * gg + 2 * j : 128 + 16 * gg + 2 * (j - 8);
+  });
+}
+
+// =====================================================================
+// launchers
+// =====================================================================
+namespace {
+
+template <typename K>
+cudaError_t set_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+template <typename T>
+cudaError_t launch_decode(const SplitParams& p, cudaStream_t stream) {
+  constexpr int WARPS = 4, NST = 4;
+  constexpr int ST = WARPS * 16;
+  const int stage = 2 * ST * kCodeBytes + 2 * ST * kScaleBytes;
+  const int epi = WARPS * 8 * kHeadDim * 4 + WARPS * 16 * 4;
+  const int bytes = max(NST * stage, epi);
+  auto kernel = nvfp4_decode_kernel<T, WARPS, NST>;
+  cudaError_t e = set_smem(kernel, bytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.num_splits, kKvHeads);
+  kernel<<<grid, WARPS * 32, bytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int NT>
+cudaError_t launch_verify_nt(const SplitParams& p, cudaStream_t stream) {
+  constexpr int NST = 3, ST = 64, NCOL = 8 * NT, WARPS = 4;
+  const int stage = 2 * ST * kCodeBytes + 2 * ST * kScaleBytes;
+  const int bytes = NST * stage + NCOL * 512 + 2 * NCOL * 128 + 2 * WARPS * NCOL * 4 + NCOL * 4;
+  auto kernel = nvfp4_verify_kernel<T, NT, NST>;
+  cudaError_t e = set_smem(kernel, bytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.num_splits, kKvHeads);
+  kernel<<<grid, 128, bytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_verify(const SplitParams& p, cudaStream_t stream) {
+  const int nt = (p.q_len * kGroup + 7) / 8;
+  switch (nt) {
+    case 1:
+    case 2: return launch_verify_nt<T, 2>(p, stream);
+    case 3: return launch_verify_nt<T, 3>(p, stream);
+    case 4: return launch_verify_nt<T, 4>(p, stream);
+    case 5: return launch_verify_nt<T, 5>(p, stream);
+    case 6: return launch_verify_nt<T, 6>(p, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream) {
+  if (p.q_len == 1) {
+    return dtype == kDtypeBF16 ? launch_decode<__nv_bfloat16>(p, stream)
+                               : launch_decode<__half>(p, stream);
+  }
+  return dtype == kDtypeBF16 ? launch_verify<__nv_bfloat16>(p, stream)
+                             : launch_verify<__half>(p, stream);
+}
+
+cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream) {
+  constexpr int WARPS = 4, NST = 3;
+  constexpr int ST = WARPS * 16;
+  const int stage = 2 * ST * kHeadDim;
+  const int epi = WARPS * 8 * kHeadDim * 4 + WARPS * 16 * 4;
+  const int bytes = max(NST * stage, epi);
+  auto kernel = fp8_decode_kernel<WARPS, NST>;
+  cudaError_t e = set_smem(kernel, bytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.num_splits, kKvHeads);
+  kernel<<<grid, WARPS * 32, bytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace qwz

@@ -1,0 +1,391 @@
+// extern "C" entry points declared in include/qwz_b200.h: argument checks,
+// launch-parameter packing, error reporting.  Nothing here allocates device
+// memory or synchronises (except qwz_device_error, a diagnostic).
+
+#include "qwz_common.cuh"
+#include "qwz_kernels.h"
+#include "../../include/qwz_b200.h"
+
+#include <cmath>
+#include <cstdio>
+#include <string>
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, const char* detail = nullptr) {
+  char buf[512];
+  if (detail)
+    std::snprintf(buf, sizeof(buf), fmt, detail);
+  else
+    std::snprintf(buf, sizeof(buf), "%s", fmt);
+  g_last_error = buf;
+  return code;
+}
+
+int launched(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return QWZ_OK;
+  char buf[512];
+  std::snprintf(buf, sizeof(buf), "%s: launch failed: %s", what, cudaGetErrorString(e));
+  g_last_error = buf;
+  return QWZ_ELAUNCH;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+int check_dtype(int32_t dtype) {
+  if (dtype != QWZ_DTYPE_F16 && dtype != QWZ_DTYPE_BF16)
+    return fail(QWZ_EINVAL, "dtype must be QWZ_DTYPE_F16 (0) or QWZ_DTYPE_BF16 (1)");
+  return QWZ_OK;
+}
+
+int check_nvfp4_cache(const void* kc, const void* vc, const void* ks, const void* vs,
+                      int32_t num_pages) {
+  if (!kc || !vc || !ks || !vs)
+    return fail(QWZ_EINVAL, "NVFP4 caches and block scales are required (non-null)");
+  if (!aligned(kc, 16) || !aligned(vc, 16) || !aligned(ks, 16) || !aligned(vs, 16))
+    return fail(QWZ_EINVAL, "NVFP4 caches and scales must be 16-byte aligned");
+  if (num_pages <= 0) return fail(QWZ_EINVAL, "num_pages must be positive");
+  if ((long long)num_pages * qwz::kPage * qwz::kKvHeads > 0x7fffffffLL)
+    return fail(QWZ_EINVAL, "num_pages too large for 32-bit token rows");
+  return QWZ_OK;
+}
+
+int fill_split(qwz::SplitParams& p, const void* q, const void* kc, const void* vc,
+               const void* ks, const void* vs, const int32_t* table, const int32_t* seqlens,
+               float* po, float* pml, int32_t table_width, int32_t num_pages, int32_t q_len,
+               int32_t num_splits, int32_t split_len, float sm_scale) {
+  if (!q || !aligned(q, 16)) return fail(QWZ_EINVAL, "q must be a non-null 16-byte aligned pointer");
+  int rc = check_nvfp4_cache(kc, vc, ks, vs, num_pages);
+  if (rc) return rc;
+  if (!table || !seqlens) return fail(QWZ_EINVAL, "block_table and cache_seqlens are required");
+  if (!po || !pml || !aligned(po, 16) || !aligned(pml, 8))
+    return fail(QWZ_EINVAL, "partial_o (16-byte aligned) and partial_ml are required");
+  if (table_width <= 0) return fail(QWZ_EINVAL, "num_pages_per_seq (table width) must be positive");
+  if (q_len < 1 || q_len > 8) return fail(QWZ_EINVAL, "q_len must be in 1..8");
+  if (num_splits < 1 || num_splits > 65535) return fail(QWZ_EINVAL, "num_splits must be in 1..65535");
+  if (split_len < 0 || split_len % qwz::kPage != 0)
+    return fail(QWZ_EINVAL, "split_len must be 0 or a positive multiple of 256");
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return fail(QWZ_EINVAL, "sm_scale must be positive and finite");
+  p = qwz::SplitParams{};
+  p.q = q;
+  p.k_codes = static_cast<const uint8_t*>(kc);
+  p.v_codes = static_cast<const uint8_t*>(vc);
+  p.k_scales = static_cast<const uint8_t*>(ks);
+  p.v_scales = static_cast<const uint8_t*>(vs);
+  p.block_table = table;
+  p.seqlens = seqlens;
+  p.partial_o = po;
+  p.partial_ml = pml;
+  p.table_width = table_width;
+  p.table_page_offset = 0;
+  p.num_pages = num_pages;
+  p.capacity = 0;
+  p.q_len = q_len;
+  p.len_add = q_len;
+  p.tok_begin = 0;
+  p.tok_span = 0x7fffffff;
+  p.split_len = split_len;
+  p.num_splits = num_splits;
+  p.sm_scale_log2 = sm_scale * kLog2e;
+  return QWZ_OK;
+}
+
+qwz::CombineParams split_combine_params(const float* po, const float* pml, int rows, int splits,
+                                        void* out) {
+  qwz::CombineParams c{};
+  c.po = po;
+  c.pml = pml;
+  c.o_row = (long long)splits * qwz::kHeadDim;
+  c.o_split = qwz::kHeadDim;
+  c.ml_row = (long long)splits * 2;
+  c.ml_split = 2;
+  c.rows = rows;
+  c.num_splits = splits;
+  c.out = out;
+  return c;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qwz_version(void) { return "qwz_b200 0.1 sm_100a"; }
+
+const char* qwz_last_error(void) { return g_last_error.c_str(); }
+
+int qwz_device_error(int32_t* out, int32_t clear) {
+  if (!out) return fail(QWZ_EINVAL, "out is null");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, qwz::g_qwz_device_error, sizeof(int));
+  if (e != cudaSuccess) return launched(e, "qwz_device_error");
+  *out = v;
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(qwz::g_qwz_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return launched(e, "qwz_device_error");
+  }
+  return QWZ_OK;
+}
+
+int qwz_nvfp4_append(const void* k, const void* v, void* k_cache, void* v_cache, void* k_scales,
+                     void* v_scales, const int32_t* block_table, const int32_t* cache_seqlens,
+                     int32_t table_width, int32_t append_len, int32_t num_kv_heads,
+                     int32_t page_size, int32_t head_dim, int32_t num_pages, int32_t dtype,
+                     void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (page_size != qwz::kPage || head_dim != qwz::kHeadDim || num_kv_heads != qwz::kKvHeads)
+    return fail(QWZ_EINVAL, "NVFP4 writer is pinned to page 256, head_dim 256, 4 KV heads");
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
+    return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+  rc = check_nvfp4_cache(k_cache, v_cache, k_scales, v_scales, num_pages);
+  if (rc) return rc;
+  if (!block_table || !cache_seqlens) return fail(QWZ_EINVAL, "block_table and cache_seqlens are required");
+  if (table_width <= 0) return fail(QWZ_EINVAL, "table_width must be positive");
+  if (append_len < 0) return fail(QWZ_EINVAL, "append_len must be non-negative");
+  qwz::AppendParams p{};
+  p.k = k;
+  p.v = v;
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.k_scales = static_cast<uint8_t*>(k_scales);
+  p.v_scales = static_cast<uint8_t*>(v_scales);
+  p.block_table = block_table;
+  p.seqlens = cache_seqlens;
+  p.table_width = table_width;
+  p.table_page_offset = 0;
+  p.append_len = append_len;
+  p.num_kv_heads = num_kv_heads;
+  p.num_pages = num_pages;
+  p.skip_foreign = 0;
+  return launched(qwz::launch_nvfp4_append(p, dtype, as_stream(stream)), "qwz_nvfp4_append");
+}
+
+int qwz_nvfp4_append_shard(const void* k, const void* v, void* k_cache, void* v_cache,
+                           void* k_scales, void* v_scales, const int32_t* block_table,
+                           const int32_t* cache_seqlens, int32_t table_width,
+                           int32_t table_page_offset, int32_t append_len, int32_t num_pages,
+                           int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
+    return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+  rc = check_nvfp4_cache(k_cache, v_cache, k_scales, v_scales, num_pages);
+  if (rc) return rc;
+  if (!block_table || !cache_seqlens) return fail(QWZ_EINVAL, "block_table and cache_seqlens are required");
+  if (table_width <= 0 || table_page_offset < 0) return fail(QWZ_EINVAL, "bad table width/offset");
+  if (append_len < 0) return fail(QWZ_EINVAL, "append_len must be non-negative");
+  qwz::AppendParams p{};
+  p.k = k;
+  p.v = v;
+  p.k_cache = static_cast<uint8_t*>(k_cache);
+  p.v_cache = static_cast<uint8_t*>(v_cache);
+  p.k_scales = static_cast<uint8_t*>(k_scales);
+  p.v_scales = static_cast<uint8_t*>(v_scales);
+  p.block_table = block_table;
+  p.seqlens = cache_seqlens;
+  p.table_width = table_width;
+  p.table_page_offset = table_page_offset;
+  p.append_len = append_len;
+  p.num_kv_heads = qwz::kKvHeads;
+  p.num_pages = num_pages;
+  p.skip_foreign = 1;
+  return launched(qwz::launch_nvfp4_append(p, dtype, as_stream(stream)), "qwz_nvfp4_append_shard");
+}
+
+int qwz_attn_split(const void* q, const void* k_cache, const void* v_cache,
+                   const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                   float* partial_o, float* partial_ml, const void* k_scales, const void* v_scales,
+                   const void* h32, int32_t split_len, int32_t num_pages_per_seq,
+                   int32_t num_splits, const void* sinks, void* global_scratch,
+                   void* profile_scratch, int32_t q_len, int32_t num_pages, float sm_scale,
+                   int32_t dtype, void* stream) {
+  (void)out;
+  (void)global_scratch;
+  (void)profile_scratch;
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (h32 || sinks)
+    return fail(QWZ_EINVAL, "h32 and sinks belong to the K8/V4 cache; they must be NULL for NVFP4");
+  qwz::SplitParams p;
+  rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                  partial_o, partial_ml, num_pages_per_seq, num_pages, q_len, num_splits,
+                  split_len, sm_scale);
+  if (rc) return rc;
+  return launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_attn_split");
+}
+
+int qwz_attn_combine(const float* partial_o, const float* partial_ml, void* out, const void* h32,
+                     int32_t num_splits, const void* sinks, int32_t q_len, int32_t dtype,
+                     void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (h32 || sinks) return fail(QWZ_EINVAL, "h32 and sinks must be NULL for NVFP4");
+  if (!partial_o || !partial_ml || !out) return fail(QWZ_EINVAL, "partial_o, partial_ml and out are required");
+  if (!aligned(partial_o, 8) || !aligned(partial_ml, 4)) return fail(QWZ_EINVAL, "misaligned partials");
+  if (q_len < 1 || q_len > 8) return fail(QWZ_EINVAL, "q_len must be in 1..8");
+  if (num_splits < 1 || num_splits > 65535) return fail(QWZ_EINVAL, "num_splits must be in 1..65535");
+  const qwz::CombineParams c =
+      split_combine_params(partial_o, partial_ml, q_len * qwz::kQHeads, num_splits, out);
+  return launched(qwz::launch_combine(c, qwz::kCombineFinal, dtype, as_stream(stream)), "qwz_attn_combine");
+}
+
+int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache, void* v_cache,
+                     void* k_scales, void* v_scales, const int32_t* block_table,
+                     const int32_t* cache_seqlens, void* out, float* partial_o, float* partial_ml,
+                     int32_t table_width, int32_t num_pages, int32_t q_len, int32_t num_splits,
+                     float sm_scale, int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!out) return fail(QWZ_EINVAL, "out is required");
+  qwz::SplitParams p;
+  rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                  partial_o, partial_ml, table_width, num_pages, q_len, num_splits, 0, sm_scale);
+  if (rc) return rc;
+  rc = qwz_nvfp4_append(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                        table_width, q_len, qwz::kKvHeads, qwz::kPage, qwz::kHeadDim, num_pages,
+                        dtype, stream);
+  if (rc) return rc;
+  rc = launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_nvfp4_attend(split)");
+  if (rc) return rc;
+  const qwz::CombineParams c =
+      split_combine_params(partial_o, partial_ml, q_len * qwz::kQHeads, num_splits, out);
+  return launched(qwz::launch_combine(c, qwz::kCombineFinal, dtype, as_stream(stream)),
+                  "qwz_nvfp4_attend(combine)");
+}
+
+int qwz_attn_shard_partial(const void* q, const void* k_cache, const void* v_cache,
+                           const void* k_scales, const void* v_scales, const int32_t* block_table,
+                           const int32_t* cache_seqlens, float* partial_o, float* partial_ml,
+                           float* send_buf, int32_t table_width, int32_t num_pages,
+                           int32_t tok_begin, int32_t tok_span, int32_t q_len, int32_t num_splits,
+                           float sm_scale, int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!send_buf || !aligned(send_buf, 8)) return fail(QWZ_EINVAL, "send_buf must be non-null and 8-byte aligned");
+  if (tok_begin < 0 || tok_begin % qwz::kPage != 0) return fail(QWZ_EINVAL, "tok_begin must be a non-negative multiple of 256");
+  if (tok_span <= 0) return fail(QWZ_EINVAL, "tok_span must be positive");
+  qwz::SplitParams p;
+  rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                  partial_o, partial_ml, table_width, num_pages, q_len, num_splits, 0, sm_scale);
+  if (rc) return rc;
+  p.tok_begin = tok_begin;
+  p.tok_span = tok_span;
+  p.table_page_offset = tok_begin / qwz::kPage;
+  rc = launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_attn_shard_partial(split)");
+  if (rc) return rc;
+  const qwz::CombineParams c =
+      split_combine_params(partial_o, partial_ml, q_len * qwz::kQHeads, num_splits, send_buf);
+  return launched(qwz::launch_combine(c, qwz::kCombinePartial, dtype, as_stream(stream)),
+                  "qwz_attn_shard_partial(combine)");
+}
+
+int qwz_lse_combine_gathered(const float* gathered, void* out, int32_t world, int32_t q_len,
+                             int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!gathered || !out || !aligned(gathered, 8)) return fail(QWZ_EINVAL, "gathered (8-byte aligned) and out are required");
+  if (world < 1 || world > 65535) return fail(QWZ_EINVAL, "world must be in 1..65535");
+  if (q_len < 1 || q_len > 8) return fail(QWZ_EINVAL, "q_len must be in 1..8");
+  const int rows = q_len * qwz::kQHeads;
+  qwz::CombineParams c{};
+  c.po = gathered + 2;
+  c.pml = gathered;
+  c.o_row = qwz::kHeadDim + 2;
+  c.o_split = (long long)rows * (qwz::kHeadDim + 2);
+  c.ml_row = qwz::kHeadDim + 2;
+  c.ml_split = (long long)rows * (qwz::kHeadDim + 2);
+  c.rows = rows;
+  c.num_splits = world;
+  c.out = out;
+  return launched(qwz::launch_combine(c, qwz::kCombineFinal, dtype, as_stream(stream)),
+                  "qwz_lse_combine_gathered");
+}
+
+int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const float* k_scale,
+                         const float* v_scale, const int32_t* length, float* part, float* stat,
+                         void* out, int32_t splits, int32_t capacity, void* stream) {
+  if (!q || !aligned(q, 16)) return fail(QWZ_EINVAL, "q must be non-null and 16-byte aligned");
+  if (!k8 || !v8 || !aligned(k8, 16) || !aligned(v8, 16)) return fail(QWZ_EINVAL, "k8 and v8 must be non-null and 16-byte aligned");
+  if (!length || !part || !stat || !out) return fail(QWZ_EINVAL, "length, part, stat and out are required");
+  if (!aligned(part, 16) || !aligned(stat, 8)) return fail(QWZ_EINVAL, "misaligned part/stat");
+  if (splits < 1 || splits > 65535) return fail(QWZ_EINVAL, "splits must be in 1..65535");
+  if (capacity <= 0 || (long long)capacity * qwz::kKvHeads > 0x7fffffffLL) return fail(QWZ_EINVAL, "capacity out of range");
+  qwz::SplitParams p{};
+  p.q = q;
+  p.k_codes = static_cast<const uint8_t*>(k8);
+  p.v_codes = static_cast<const uint8_t*>(v8);
+  p.k_page_scale = k_scale;
+  p.v_page_scale = v_scale;
+  p.seqlens = length;
+  p.partial_o = part;
+  p.partial_ml = stat;
+  p.capacity = capacity;
+  p.q_len = 1;
+  p.len_add = 0;
+  p.tok_begin = 0;
+  p.tok_span = capacity;
+  p.split_len = 0;
+  p.num_splits = splits;
+  p.sm_scale_log2 = (1.0f / 16.0f) * kLog2e;
+  int rc = launched(qwz::launch_fp8_split(p, as_stream(stream)), "qwz_fp8_draft_decode(split)");
+  if (rc) return rc;
+  const qwz::CombineParams c = split_combine_params(part, stat, qwz::kQHeads, splits, out);
+  return launched(qwz::launch_combine(c, qwz::kCombineFinal, QWZ_DTYPE_F16, as_stream(stream)),
+                  "qwz_fp8_draft_decode(combine)");
+}
+
+int qwz_fp8_shadow_write(const void* k, const void* v, void* k8, void* v8, const float* k_scale,
+                         const float* v_scale, const int32_t* position, int32_t capacity,
+                         int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16)) return fail(QWZ_EINVAL, "k and v must be non-null and 16-byte aligned");
+  if (!k8 || !v8 || !aligned(k8, 8) || !aligned(v8, 8)) return fail(QWZ_EINVAL, "k8 and v8 must be non-null and 8-byte aligned");
+  if (!position) return fail(QWZ_EINVAL, "position is required");
+  if (capacity <= 0) return fail(QWZ_EINVAL, "capacity must be positive");
+  qwz::Fp8WriteParams p{};
+  p.k = k;
+  p.v = v;
+  p.k8 = static_cast<uint8_t*>(k8);
+  p.v8 = static_cast<uint8_t*>(v8);
+  p.k_page_scale = k_scale;
+  p.v_page_scale = v_scale;
+  p.position = position;
+  p.capacity = capacity;
+  p.num_kv_heads = qwz::kKvHeads;
+  return launched(qwz::launch_fp8_write(p, dtype, as_stream(stream)), "qwz_fp8_shadow_write");
+}
+
+int qwz_nvfp4_gather(const void* packed, const void* scales, const int32_t* block_table,
+                     const int32_t* seq_lens, void* output, int32_t batch, int32_t max_tokens,
+                     int32_t table_width, int32_t n_heads, int32_t head_dim, int32_t page_size,
+                     void* stream) {
+  if (!packed || !scales || !block_table || !seq_lens || !output)
+    return fail(QWZ_EINVAL, "all pointers are required");
+  if (!aligned(packed, 4) || !aligned(output, 16)) return fail(QWZ_EINVAL, "packed must be 4-byte and output 16-byte aligned");
+  if (batch < 0 || max_tokens < 0 || table_width <= 0 || n_heads <= 0 || page_size <= 0)
+    return fail(QWZ_EINVAL, "sizes must be positive");
+  if (head_dim <= 0 || head_dim % 16 != 0) return fail(QWZ_EINVAL, "head_dim must be a positive multiple of 16");
+  qwz::GatherParams p{};
+  p.packed = static_cast<const uint8_t*>(packed);
+  p.scales = static_cast<const uint8_t*>(scales);
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.out = static_cast<__half*>(output);
+  p.batch = batch;
+  p.max_tokens = max_tokens;
+  p.table_width = table_width;
+  p.n_heads = n_heads;
+  p.head_dim = head_dim;
+  p.page_size = page_size;
+  return launched(qwz::launch_nvfp4_gather(p, as_stream(stream)), "qwz_nvfp4_gather");
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+// Host-side launch interface of the sm_100a kernels (internal; the public
+// C ABI is include/qwz_b200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace qwz {
+
+enum : int { kDtypeF16 = 0, kDtypeBF16 = 1 };
+
+// Split-K attention launch (NVFP4 paged decode/verify, FP8 draft decode).
+struct SplitParams {
+  const void* q;                 // [q_len, 24, 256] FP16/BF16
+  const uint8_t* k_codes;        // NVFP4: [P,256,4,128] ; FP8: [T,4,256] E4M3
+  const uint8_t* v_codes;
+  const uint8_t* k_scales;       // NVFP4: [P,256,4,16] E4M3 ; FP8: unused
+  const uint8_t* v_scales;
+  const float* k_page_scale;     // FP8: [ceil(T/256), 4] FP32 or null (= 1)
+  const float* v_page_scale;
+  const int32_t* block_table;    // NVFP4: logical page -> physical page
+  const int32_t* seqlens;        // device length word [1]
+  float* partial_o;              // [R, num_splits, 256]
+  float* partial_ml;             // [R, num_splits, 2]  (m in log2 units, l)
+  int table_width;               // entries of block_table
+  int table_page_offset;         // logical page index of block_table[0]
+  int num_pages;                 // physical pages in the NVFP4 pool
+  int capacity;                  // FP8: token slots in the store
+  int q_len;                     // query rows per head (1..8)
+  int len_add;                   // valid length = seqlens[0] + len_add
+  int tok_begin;                 // first logical token of this launch (multiple of 256)
+  int tok_span;                  // tokens this launch may cover
+  int split_len;                 // >0: fixed tokens per split (multiple of 256); 0: balanced
+  int num_splits;
+  float sm_scale_log2;           // sm_scale * log2(e)
+};
+
+// LSE combine of split partials.  Row r, split s reads
+//   m,l at pml[r*ml_row + s*ml_split + {0,1}] and O at po[r*o_row + s*o_split + d].
+struct CombineParams {
+  const float* po;
+  const float* pml;
+  long long o_row, o_split, ml_row, ml_split;
+  int rows;
+  int num_splits;
+  void* out;          // final: [rows, 256] FP16/BF16 ; partial: [rows, 258] FP32 (m, l, O)
+};
+
+enum : int { kCombineFinal = 0, kCombinePartial = 1 };
+
+struct AppendParams {
+  const void* k;                 // [S, kv_heads, 256] new rows
+  const void* v;
+  uint8_t* k_cache;              // [P, 256, kv_heads, 128]
+  uint8_t* v_cache;
+  uint8_t* k_scales;             // [P, 256, kv_heads, 16] E4M3
+  uint8_t* v_scales;
+  const int32_t* block_table;
+  const int32_t* seqlens;        // pre-append length [1]
+  int table_width;
+  int table_page_offset;
+  int append_len;
+  int num_kv_heads;
+  int num_pages;
+  int skip_foreign;              // rows outside this table's pages: skip silently (shards)
+};
+
+struct Fp8WriteParams {
+  const void* k;                 // [kv_heads, 256] one new row (FP16/BF16)
+  const void* v;
+  uint8_t* k8;                   // [capacity, kv_heads, 256] E4M3
+  uint8_t* v8;
+  const float* k_page_scale;     // [pages, kv_heads] or null (= 1)
+  const float* v_page_scale;
+  const int32_t* position;       // slot to write [1]
+  int capacity;
+  int num_kv_heads;
+};
+
+struct GatherParams {
+  const uint8_t* packed;         // [P, page, heads, dim/2]
+  const uint8_t* scales;         // [P, page, heads, dim/16] E4M3
+  const int32_t* block_table;    // [batch, table_width]
+  const int32_t* seq_lens;       // [batch]
+  __half* out;                   // [batch, max_tokens, heads, dim]
+  int batch, max_tokens, table_width, n_heads, head_dim, page_size;
+};
+
+cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream);
+cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStream_t stream);
+cudaError_t launch_nvfp4_append(const AppendParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_fp8_write(const Fp8WriteParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_nvfp4_gather(const GatherParams& p, cudaStream_t stream);
+
+}  // namespace qwz

@@ -1,0 +1,49 @@
+"""One-row decode attention for the MTP proposer over the FP8 shadow KV.
+
+Drop-in for engine/forward/draft_attention.py:82-108 (`DecodeAttention`):
+the constructor allocates the split workspace once and `attend` launches the
+sm_100a split-K kernel plus the LSE combine, reading the length from a
+device tensor, so a 6-step draft roll can be captured in one CUDA graph
+(engine/forward/draft.py:440-472).  `shadow_write` replaces the FP8 shadow
+update of draft.py:359-366.  Optional per-(256-token page, KV head) FP32
+scales generalise the reference's unscaled `_fp8` shadow (scale 1).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+SPLITS = 16
+KV_HEADS = 4
+DIM = 256
+
+
+class DecodeAttention:
+    """Reusable workspace; `attend` launches two kernels and allocates nothing."""
+
+    def __init__(self, heads=24, kv_heads=4, dim=256, device="cuda", splits: int = SPLITS):
+        if (heads, kv_heads, dim) != (24, 4, 256):
+            raise ValueError("draft attention is pinned to 24/4 heads, head_dim 256")
+        self.heads = heads
+        self.kv_heads = kv_heads
+        self.dim = dim
+        self.group = heads // kv_heads
+        self.splits = int(splits)
+        self.part = torch.empty(heads * self.splits * dim, dtype=torch.float32, device=device)
+        self.stat = torch.empty(heads * self.splits * 2, dtype=torch.float32, device=device)
+
+    def attend(self, query, k_store, v_store, length, out, k_scale=None, v_scale=None):
+        """query [1,1,H,D] FP16; stores [1,T,KV,D] E4M3; length int32 [1]
+        (keys [0, length) are attended); out [1,1,H,D] FP16."""
+        for t in (k_store, v_store):
+            if t.dtype not in (torch.float8_e4m3fn, torch.uint8):
+                raise NotImplementedError("the B200 draft kernel reads the FP8 E4M3 shadow store")
+        ops.fp8_draft_decode(query, k_store, v_store, length, self.part, self.stat, out,
+                             self.splits, k_scale, v_scale)
+        return out
+
+
+def shadow_write(key, value, k8, v8, position, k_scale=None, v_scale=None):
+    """FP8 shadow update at slot position[0]: E4M3(clamp(x / scale, +-448))."""
+    ops.fp8_shadow_write(key, value, k8, v8, position, k_scale, v_scale)
