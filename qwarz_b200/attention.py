@@ -36,6 +36,10 @@ HEAD_DIM = 256
 PAGE = 256
 
 
+def _capturing() -> bool:
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
 @dataclass
 class AttnArgs:
     """The ExLlamaV3 `AttnArgs` fields the reference adapter reads
@@ -193,7 +197,7 @@ class NVFP4AttentionAdapter:
         key = (q_len, str(args.q.device))
         ws = state.workspaces.get(key)
         if ws is None:
-            if torch.cuda.is_current_stream_capturing():
+            if _capturing():
                 raise RuntimeError("split workspace must exist before CUDA graph capture")
             splits = ops.default_splits(args.q.device, max_tokens, q_len)
             ws = (splits, *ops.split_workspace(args.q.device, q_len, splits))
@@ -203,7 +207,7 @@ class NVFP4AttentionAdapter:
     def _output(self, state: _LayerState, args) -> torch.Tensor:
         out = state.outputs.get(args.q_len)
         if out is None or out.dtype != args.q.dtype or out.device != args.q.device:
-            if torch.cuda.is_current_stream_capturing():
+            if _capturing():
                 raise RuntimeError("attention output must exist before CUDA graph capture")
             out = torch.empty_like(args.q)
             state.outputs[args.q_len] = out
@@ -225,7 +229,7 @@ class NVFP4AttentionAdapter:
         causal, as xqa.py:662)."""
         ops.nvfp4_append(args.k, args.v, args.k_cache, args.v_cache, args.k_scales,
                          args.v_scales, args.block_table, args.cache_seqlens)
-        out = torch.empty_like(args.q) if not torch.cuda.is_current_stream_capturing() else self._output(state, args)
+        out = torch.empty_like(args.q) if not _capturing() else self._output(state, args)
         windows = math.ceil(args.q_len / XQA_MAX_QUERY)
         if state.prefill_lens is None or state.prefill_lens.numel() < windows:
             state.prefill_lens = torch.empty(max(windows, 16), dtype=torch.int32, device=args.q.device)
@@ -276,6 +280,8 @@ class NVFP4AttentionAdapter:
         if args.k_scales is None:
             return None  # non-NVFP4 attention falls through (xqa.py:777-779)
         append_len = self._validate_nvfp4(args)
+        if not args.q.is_cuda:
+            raise ValueError("qwarz_b200 operators run on CUDA tensors only (no CPU fallback)")
         self.max_observed_query = max(self.max_observed_query, args.q_len)
         state = self._layer_state(args)
         if args.q_len > XQA_MAX_QUERY:
@@ -284,7 +290,7 @@ class NVFP4AttentionAdapter:
             self.routes["prefill_windows"] += 1
             self.query_rows["prefill_windows"] += args.q_len
             return out
-        if self.decode_graphs and not torch.cuda.is_current_stream_capturing():
+        if self.decode_graphs and not _capturing():
             key = (args.q_len, float(args.sm_scale), args.q.dtype)
             g = state.graphs.get(key)
             if g is not None and not g.matches(args):

