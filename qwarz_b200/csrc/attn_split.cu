@@ -217,7 +217,7 @@ QWZ_DEVINL PFrag softmax_step_decode(float (&t)[4], float& m0, float& m1, float&
 template <int WARPS, class DMap>
 QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, int kvh,
                                 float m0, float m1, float l0, float l1,
-                                const float (&o)[16][4], DMap dmap) {
+                                const float (&o)[16][4], bool consumer, DMap dmap) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
@@ -226,21 +226,23 @@ QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, 
   }
   float* red = reinterpret_cast<float*>(smem);          // [WARPS][8][256]
   float* mlred = red + WARPS * 8 * kHeadDim;              // [WARPS][8][2]
-  float* ow = red + warp * 8 * kHeadDim;
+  if (consumer) {
+    float* ow = red + warp * 8 * kHeadDim;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int d = dmap(g, j);
-    *reinterpret_cast<float2*>(ow + (2 * qd) * kHeadDim + d) = make_float2(o[j][0], o[j][2]);
-    *reinterpret_cast<float2*>(ow + (2 * qd + 1) * kHeadDim + d) = make_float2(o[j][1], o[j][3]);
-  }
-  if (g == 0) {
-    mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
-    mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
-    mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
-    mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
+    for (int j = 0; j < 16; ++j) {
+      const int d = dmap(g, j);
+      *reinterpret_cast<float2*>(ow + (2 * qd) * kHeadDim + d) = make_float2(o[j][0], o[j][2]);
+      *reinterpret_cast<float2*>(ow + (2 * qd + 1) * kHeadDim + d) = make_float2(o[j][1], o[j][3]);
+    }
+    if (g == 0) {
+      mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
+      mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
+      mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
+      mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
+    }
   }
   __syncthreads();
-  for (int idx = tid; idx < kGroup * kHeadDim; idx += WARPS * 32) {
+  for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
     const int col = idx >> 8, d = idx & 255;
     float M = -CUDART_INF_F;
 #pragma unroll
@@ -268,72 +270,94 @@ QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, 
 // =====================================================================
 // NVFP4 decode, q_len = 1.
 // =====================================================================
+// Warp WARPS is the producer: its lane 0 streams 64-token stages of one KV
+// head (codes and scales of K and V, four TMA boxes, 18 KB) into an
+// NST-deep ring guarded by full/empty mbarriers.  Warps 0..WARPS-1 consume:
+// warp w owns tokens 16w..16w+15 of every stage.  No CTA-wide barrier runs
+// inside the loop.
 template <typename T, int WARPS, int NST>
-__global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const SplitParams p) {
+__global__ void __launch_bounds__((WARPS + 1) * 32, 2)
+    nvfp4_decode_kernel(const __grid_constant__ SplitParams p) {
   constexpr int ST = WARPS * 16;
   constexpr int CODE_TILE = ST * kCodeBytes;
   constexpr int SCALE_TILE = ST * kScaleBytes;
   constexpr int STAGE_BYTES = 2 * CODE_TILE + 2 * SCALE_TILE;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const uint32_t sbase = smem_u32(smem);
+  // TMA boxes with the 128-byte swizzle need 1024-byte aligned destinations
+  const uint32_t sbase = (smem_u32(smem) + 1023u) & ~1023u;
+  const uint32_t bar_full = sbase + NST * STAGE_BYTES;
+  const uint32_t bar_empty = bar_full + 8 * NST;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y;
 
   const StageRange rg = stage_range<ST>(p, split);
 
-  uint32_t qf[32];
-  float cf0, cf1;
-  load_q_decode<T>(reinterpret_cast<const T*>(p.q), g < kGroup ? kvh * kGroup + g : -1, qd,
-                   p.sm_scale_log2, qf, cf0, cf1);
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, WARPS);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
 
   float o[16][4];
 #pragma unroll
   for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
+  const bool consumer = warp < WARPS;
 
-  const uint8_t* kc = p.k_codes;
-  const uint8_t* vc = p.v_codes;
-  const uint8_t* ks = p.k_scales;
-  const uint8_t* vs = p.v_scales;
-
-  auto issue = [&](int k) {
-    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
-    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
-    const int pp = lookup_page(p, t0, tid == 0);
-    const size_t rowbase = (size_t)(pp < 0 ? 0 : pp) * kPage + (t0 & (kPage - 1));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int idx = tid + (i & 3) * (2 * ST);
-      const int row = idx >> 3, ch = idx & 7;
-      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
-      const uint8_t* base = (i < 4) ? kc : vc;
-      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kCodeBytes + ch * 16 : base;
-      cp_async16(slot + (i >> 2) * CODE_TILE + swz128(row, ch), src, ok ? 16u : 0u);
+  if (!consumer) {
+    if (lane == 0 && rg.n_st > 0) {
+      tma_prefetch_desc(&p.tm_kc);
+      tma_prefetch_desc(&p.tm_vc);
+      tma_prefetch_desc(&p.tm_ks);
+      tma_prefetch_desc(&p.tm_vs);
+      int issued = 0;
+      for (int k = 0; k < rg.n_st; ++k) {
+        const int slot = k % NST;
+        if (k >= NST && !mbar_wait(bar_empty + 8 * slot, ((k / NST) - 1) & 1)) {
+          flag_error(kErrTimeout);
+          break;
+        }
+        const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
+        const int pp = lookup_page(p, t0, true);
+        const uint32_t fb = bar_full + 8 * slot, dst = sbase + slot * STAGE_BYTES;
+        ++issued;
+        if (pp < 0) {  // bad page id: no copy; consumers mask the whole stage
+          mbar_arrive(fb);
+          continue;
+        }
+        mbar_arrive_expect_tx(fb, STAGE_BYTES);
+        const int y = pp * kPage + (t0 & (kPage - 1));
+        tma_load_2d(dst, &p.tm_kc, kvh * kCodeBytes, y, fb);
+        tma_load_2d(dst + CODE_TILE, &p.tm_vc, kvh * kCodeBytes, y, fb);
+        tma_load_2d(dst + 2 * CODE_TILE, &p.tm_ks, kvh * kScaleBytes, y, fb);
+        tma_load_2d(dst + 2 * CODE_TILE + SCALE_TILE, &p.tm_vs, kvh * kScaleBytes, y, fb);
+      }
+      // never leave with copies in flight (only matters after a timeout)
+      for (int k = max(0, issued - NST); k < issued; ++k)
+        if (!mbar_wait(bar_full + 8 * (k % NST), (k / NST) & 1)) flag_error(kErrTimeout);
     }
-    {
-      const int tensor = tid >= ST ? 1 : 0;
-      const int row = tid - tensor * ST;
-      const bool ok = pp >= 0 && (t0 + row) < rg.tok_end;
-      const uint8_t* base = tensor ? vs : ks;
-      const uint8_t* src = ok ? base + ((rowbase + row) * kKvHeads + kvh) * kScaleBytes : base;
-      cp_async16(slot + 2 * CODE_TILE + tensor * SCALE_TILE + row * 16, src, ok ? 16u : 0u);
-    }
-  };
-
-#pragma unroll
-  for (int k = 0; k < NST - 1; ++k) {
-    if (k < rg.n_st) issue(k);
-    cp_async_commit();
   }
 
-  for (int k = 0; k < rg.n_st; ++k) {
-    cp_async_wait<NST - 2>();
-    __syncthreads();
-    if (k + NST - 1 < rg.n_st) issue(k + NST - 1);
-    cp_async_commit();
+  uint32_t qf[32];
+  float cf0 = 0.f, cf1 = 0.f;
+  if (consumer)
+    load_q_decode<T>(reinterpret_cast<const T*>(p.q), g < kGroup ? kvh * kGroup + g : -1, qd,
+                     p.sm_scale_log2, qf, cf0, cf1);
 
-    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
-    const int tw0 = p.tok_begin + (rg.st_lo + k) * ST + 16 * warp;
+  for (int k = 0; consumer && k < rg.n_st; ++k) {
+    const int slot_i = k % NST;
+    if (!mbar_wait(bar_full + 8 * slot_i, (k / NST) & 1)) {
+      flag_error(kErrTimeout);
+      break;
+    }
+    const uint32_t slot = sbase + slot_i * STAGE_BYTES;
+    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
+    const int valid_end = lookup_page(p, t0, false) >= 0 ? rg.tok_end : t0;
+    const int tw0 = t0 + 16 * warp;
 
     // ---------------- S^T = K Q^T over the 16 tokens of this warp
     const int r0 = 16 * warp + g, r1 = r0 + 8;
@@ -369,9 +393,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const Split
     }
     float t[4] = {(sa[0] + sb[0]) * cf0, (sa[1] + sb[1]) * cf1, (sa[2] + sb[2]) * cf0,
                   (sa[3] + sb[3]) * cf1};
-    if (tw0 + 16 > rg.tok_end) {
-      if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
-      if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
+    const bool tail = tw0 + 16 > valid_end;
+    if (tail) {
+      if (tw0 + g >= valid_end) t[0] = t[1] = -CUDART_INF_F;
+      if (tw0 + g + 8 >= valid_end) t[2] = t[3] = -CUDART_INF_F;
     }
     const PFrag pf = softmax_step_decode(t, m0, m1, l0, l1, o);
 
@@ -383,8 +408,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const Split
     const uint4 vcc = lds128(vbase + swz128(ra + 8, g));
     const uint4 vd = lds128(vbase + swz128(ra + 9, g));
     const uint32_t vsb = slot + 2 * CODE_TILE + SCALE_TILE + 2 * g;
-    const uint32_t sa16 = lds16(vsb + ra * 16), sb16 = lds16(vsb + (ra + 1) * 16);
-    const uint32_t sc16 = lds16(vsb + (ra + 8) * 16), sd16 = lds16(vsb + (ra + 9) * 16);
+    uint32_t sa16 = lds16(vsb + ra * 16), sb16 = lds16(vsb + (ra + 1) * 16);
+    uint32_t sc16 = lds16(vsb + (ra + 8) * 16), sd16 = lds16(vsb + (ra + 9) * 16);
+    if (tail) {  // rows past the valid end hold stale bytes: zero their scales
+      const int ta = t0 + ra;
+      if (ta >= valid_end) sa16 = 0;
+      if (ta + 1 >= valid_end) sb16 = 0;
+      if (ta + 8 >= valid_end) sc16 = 0;
+      if (ta + 9 >= valid_end) sd16 = 0;
+    }
     uint32_t spab0, spab1, spcd0, spcd1;
     e4m3x4_to_f16x2x2(__byte_perm(sa16, sb16, 0x5140), spab0, spab1);
     e4m3x4_to_f16x2x2(__byte_perm(sc16, sd16, 0x5140), spcd0, spcd1);
@@ -413,11 +445,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1) nvfp4_decode_kernel(const Split
         mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.lo0, pf.lo1);
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_empty + 8 * slot_i);
   }
 
-  cp_async_wait<0>();
   __syncthreads();
-  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o,
+  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, consumer,
                          [](int gg, int j) { return 32 * gg + 2 * j; });
 }
 
@@ -921,7 +954,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) fp8_decode_kernel(const SplitPa
 
   cp_async_wait<0>();
   __syncthreads();
-  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int gg, int j) {
+  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, true, [](int gg, int j) {
     return j < 8 ? 16 * gg + 2 * j : 128 + 16 * gg + 2 * (j - 8);
   });
 }
@@ -938,16 +971,16 @@ cudaError_t set_smem(K kernel, int bytes) {
 
 template <typename T>
 cudaError_t launch_decode(const SplitParams& p, cudaStream_t stream) {
-  constexpr int WARPS = 4, NST = 4;
+  constexpr int WARPS = 4, NST = 6;
   constexpr int ST = WARPS * 16;
   const int stage = 2 * ST * kCodeBytes + 2 * ST * kScaleBytes;
   const int epi = WARPS * 8 * kHeadDim * 4 + WARPS * 16 * 4;
-  const int bytes = max(NST * stage, epi);
+  const int bytes = max(NST * stage + 16 * NST, epi) + 1024;
   auto kernel = nvfp4_decode_kernel<T, WARPS, NST>;
   cudaError_t e = set_smem(kernel, bytes);
   if (e != cudaSuccess) return e;
   dim3 grid(p.num_splits, kKvHeads);
-  kernel<<<grid, WARPS * 32, bytes, stream>>>(p);
+  kernel<<<grid, (WARPS + 1) * 32, bytes, stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -6,8 +6,11 @@
 #include "qwz_kernels.h"
 #include "../../include/qwz_b200.h"
 
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 namespace {
@@ -56,6 +59,52 @@ int check_nvfp4_cache(const void* kc, const void* vc, const void* ks, const void
   return QWZ_OK;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library links only the static CUDA runtime).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D uint8 view [rows, row_bytes] of a pool, box box_x bytes x box_y rows.
+int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_x,
+              uint32_t box_y, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) return fail(QWZ_ELAUNCH, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[2] = {row_bytes, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_x, box_y};
+  cuuint32_t elem[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                        box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QWZ_EINVAL, "TMA descriptor encoding failed for the NVFP4 pool");
+  return QWZ_OK;
+}
+
+// Descriptors of the NVFP4 pool: codes [P*256, 512 B] (128 x 64 boxes,
+// 128-byte swizzle), scales [P*256, 64 B] (16 x 64 boxes).
+int encode_pool(qwz::SplitParams& p, int32_t num_pages) {
+  const uint64_t rows = (uint64_t)num_pages * qwz::kPage;
+  int rc = encode_2d(&p.tm_kc, p.k_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_2d(&p.tm_vc, p.v_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_2d(&p.tm_ks, p.k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = encode_2d(&p.tm_vs, p.v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+  return rc;
+}
+
 int fill_split(qwz::SplitParams& p, const void* q, const void* kc, const void* vc,
                const void* ks, const void* vs, const int32_t* table, const int32_t* seqlens,
                float* po, float* pml, int32_t table_width, int32_t num_pages, int32_t q_len,
@@ -93,7 +142,7 @@ int fill_split(qwz::SplitParams& p, const void* q, const void* kc, const void* v
   p.split_len = split_len;
   p.num_splits = num_splits;
   p.sm_scale_log2 = sm_scale * kLog2e;
-  return QWZ_OK;
+  return encode_pool(p, num_pages);
 }
 
 qwz::CombineParams split_combine_params(const float* po, const float* pml, int rows, int splits,

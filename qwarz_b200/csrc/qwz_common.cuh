@@ -32,6 +32,7 @@ enum DeviceError : int {
   kErrTableRange = 1,  // logical page beyond the block-table width
   kErrPageRange = 2,   // physical page id outside the cache pool
   kErrSlotRange = 4,   // FP8 draft slot beyond the store capacity
+  kErrTimeout = 8,     // a bounded mbarrier wait gave up
 };
 
 // Device-wide error word.  The library is one translation unit
@@ -160,7 +161,58 @@ QWZ_DEVINL void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-// 128-byte-row XOR swizzle of 16-byte chunks (rows of 128 B, chunk 0..7).
+// ------------------------------------------------------- mbarrier and TMA
+// Spin budget of a bounded mbarrier wait: iterations of try_wait, each of
+// which suspends for at most kWaitHintNs.  ~1 s in total; on expiry the
+// waiter sets kErrTimeout and gives up instead of hanging the GPU.
+constexpr int kWaitSpins = 1 << 17;
+constexpr uint32_t kWaitHintNs = 8000;
+
+QWZ_DEVINL void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+QWZ_DEVINL void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+QWZ_DEVINL void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+QWZ_DEVINL void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// Waits for the phase with the given parity; false (and kErrTimeout) if the
+// spin budget runs out.
+QWZ_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < kWaitSpins; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(kWaitHintNs)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// 2-D tiled TMA load of one box into shared memory, completing on `bar`.
+QWZ_DEVINL void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+QWZ_DEVINL void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+// 128-byte-row XOR swizzle of 16-byte chunks (rows of 128 B, chunk 0..7);
+// the layout a TMA tiled load with CU_TENSOR_MAP_SWIZZLE_128B produces in a
+// 1024-byte aligned destination.
 QWZ_DEVINL uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }

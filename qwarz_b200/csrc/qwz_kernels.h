@@ -2,6 +2,7 @@
 // C ABI is include/qwz_b200.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -11,7 +12,11 @@ namespace qwz {
 enum : int { kDtypeF16 = 0, kDtypeBF16 = 1 };
 
 // Split-K attention launch (NVFP4 paged decode/verify, FP8 draft decode).
-struct SplitParams {
+struct alignas(64) SplitParams {
+  // TMA descriptors of the NVFP4 pool viewed as 2-D byte tensors
+  // [P*256 token rows, 512 B] (codes, 128B swizzle, 128 x 64 box) and
+  // [P*256, 64 B] (scales, 16 x 64 box); filled by the host (capi.cu).
+  CUtensorMap tm_kc, tm_vc, tm_ks, tm_vs;
   const void* q;                 // [q_len, 24, 256] FP16/BF16
   const uint8_t* k_codes;        // NVFP4: [P,256,4,128] ; FP8: [T,4,256] E4M3
   const uint8_t* v_codes;
