@@ -33,426 +33,11 @@
 // the O rescale is rare.  Partials are (m, l, O) with O unnormalised and m in
 // log2 units of sm_scale * q.k.
 
-#include "qwz_common.cuh"
-#include "qwz_kernels.h"
-
-#include <math_constants.h>
+#include "attn_common.cuh"
 
 namespace qwz {
 
-namespace {
-
-constexpr float kLazy = 8.0f;
-constexpr unsigned kFull = 0xffffffffu;
-
-QWZ_DEVINL float shfl_xor(float v, int m) { return __shfl_xor_sync(kFull, v, m); }
-
-// Four E4M3 scale bytes -> four broadcast f16x2 (s_i, s_i).
-QWZ_DEVINL void scales_bcast4(uint32_t ks, uint32_t (&sc)[4]) {
-  uint32_t h01, h23;
-  e4m3x4_to_f16x2x2(ks, h01, h23);
-  sc[0] = __byte_perm(h01, 0, 0x1010);
-  sc[1] = __byte_perm(h01, 0, 0x3232);
-  sc[2] = __byte_perm(h23, 0, 0x1010);
-  sc[3] = __byte_perm(h23, 0, 0x3232);
-}
-
-// Power-of-two factor that brings a row amax into [2^14, 2^15), so a BF16
-// (or FP16) query row converts to FP16 without overflow and, apart from
-// elements below amax * 2^-24, exactly.  Returns the factor.
-QWZ_DEVINL float pow2_row_scale(float amax) {
-  int e = 0;
-  if (amax > 0.f && amax < CUDART_INF_F) frexpf(amax, &e);
-  int k = 15 - e;
-  k = k > 120 ? 120 : (k < -120 ? -120 : k);
-  return ldexpf(1.0f, k);
-}
-
-// Decode-layout Q fragments.  Lane (g, q) holds row g of the head group,
-// d in [64q, 64q+64) as 32 f16x2 words; rows 6,7 are zero padding.
-template <typename T>
-QWZ_DEVINL void load_q_decode(const T* q, int row, int qd, float sm_scale_log2,
-                              uint32_t (&qf)[32], float& cf0, float& cf1) {
-  if (row >= 0) {
-    const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)row * kHeadDim + 64 * qd);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 v = __ldg(src + i);
-      qf[4 * i + 0] = v.x;
-      qf[4 * i + 1] = v.y;
-      qf[4 * i + 2] = v.z;
-      qf[4 * i + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) qf[i] = 0u;
-  }
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float2 f = InTraits<T>::to_float2(qf[i]);
-    amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-  }
-  amax = fmaxf(amax, shfl_xor(amax, 1));
-  amax = fmaxf(amax, shfl_xor(amax, 2));
-  const float sc = pow2_row_scale(amax);
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float2 f = InTraits<T>::to_float2(qf[i]);
-    qf[i] = pack_half2(f.x * sc, f.y * sc);
-  }
-  const float rowfac = sm_scale_log2 / sc;
-  const int lane = threadIdx.x & 31;
-  (void)lane;
-  cf0 = __shfl_sync(kFull, rowfac, 4 * (2 * qd));
-  cf1 = __shfl_sync(kFull, rowfac, 4 * (2 * qd + 1));
-}
-
-// Token range of this split, in stages of ST tokens.
-struct StageRange {
-  int tok_end;  // exclusive end of the valid tokens (post-append length clipped)
-  int st_lo;
-  int n_st;
-};
-
-template <int ST>
-QWZ_DEVINL StageRange stage_range(const SplitParams& p, int split) {
-  StageRange r;
-  const int L = __ldg(p.seqlens) + p.len_add;
-  const long long end = (long long)p.tok_begin + (long long)p.tok_span;
-  r.tok_end = (int)min((long long)L, end);
-  const int n_tok = max(r.tok_end - p.tok_begin, 0);
-  const int total = (n_tok + ST - 1) / ST;
-  int lo, hi;
-  if (p.split_len > 0) {
-    const int per = p.split_len / ST;
-    lo = split * per;
-    hi = min(lo + per, total);
-  } else {
-    lo = (int)(((long long)split * total) / p.num_splits);
-    hi = (int)(((long long)(split + 1) * total) / p.num_splits);
-  }
-  r.st_lo = lo;
-  r.n_st = max(hi - lo, 0);
-  return r;
-}
-
-// Physical page of the 256-token page holding logical token t, or -1.
-QWZ_DEVINL int lookup_page(const SplitParams& p, int t, bool report) {
-  const int lp = (t >> 8) - p.table_page_offset;
-  if (lp < 0 || lp >= p.table_width) {
-    if (report) flag_error(kErrTableRange);
-    return -1;
-  }
-  const int pp = __ldg(p.block_table + lp);
-  if (pp < 0 || pp >= p.num_pages) {
-    if (report) flag_error(kErrPageRange);
-    return -1;
-  }
-  return pp;
-}
-
-// P (FP32) as two FP16 B-fragments hi + lo with hi + lo = P to ~2^-22
-// relative, so the PV product through FP16 tensor cores keeps FP32-level
-// accuracy (one extra MMA per tile, no extra dequantisation).
-struct PFrag {
-  uint32_t hi0, hi1, lo0, lo1;
-};
-
-QWZ_DEVINL PFrag p_fragments(float p0, float p1, float p2, float p3) {
-  PFrag f;
-  const uint32_t h01 = pack_half2(p0, p1), h23 = pack_half2(p2, p3);
-  const float2 r01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-  const float2 r23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  f.hi0 = movmatrix_trans(h01);
-  f.hi1 = movmatrix_trans(h23);
-  f.lo0 = movmatrix_trans(pack_half2(p0 - r01.x, p1 - r01.y));
-  f.lo1 = movmatrix_trans(pack_half2(p2 - r23.x, p3 - r23.y));
-  return f;
-}
-
-// One online-softmax step on a 16-token x 8-column S^T fragment.
-// t: scaled scores (c-fragment), overwritten with p; returns P^T fragments.
-QWZ_DEVINL PFrag softmax_step_decode(float (&t)[4], float& m0, float& m1, float& l0,
-                                     float& l1, float (&o)[16][4]) {
-  float mx0 = fmaxf(t[0], t[2]);
-  float mx1 = fmaxf(t[1], t[3]);
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    mx0 = fmaxf(mx0, shfl_xor(mx0, off));
-    mx1 = fmaxf(mx1, shfl_xor(mx1, off));
-  }
-  const bool need = (mx0 > m0 + kLazy) || (mx1 > m1 + kLazy);
-  if (__any_sync(kFull, need)) {
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float a0 = (n0 == -CUDART_INF_F) ? 1.f : exp2_approx(m0 - n0);
-    const float a1 = (n1 == -CUDART_INF_F) ? 1.f : exp2_approx(m1 - n1);
-    m0 = n0;
-    m1 = n1;
-    l0 *= a0;
-    l1 *= a1;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      o[j][0] *= a0;
-      o[j][1] *= a1;
-      o[j][2] *= a0;
-      o[j][3] *= a1;
-    }
-  }
-  const float mu0 = (m0 == -CUDART_INF_F) ? 0.f : m0;
-  const float mu1 = (m1 == -CUDART_INF_F) ? 0.f : m1;
-  const float p0 = exp2_approx(t[0] - mu0), p1 = exp2_approx(t[1] - mu1);
-  const float p2 = exp2_approx(t[2] - mu0), p3 = exp2_approx(t[3] - mu1);
-  l0 += p0 + p2;
-  l1 += p1 + p3;
-  t[0] = p0;
-  t[1] = p1;
-  t[2] = p2;
-  t[3] = p3;
-  return p_fragments(p0, p1, p2, p3);
-}
-
-// Cross-warp merge of decode-layout (m, l, O) and the partial store.
-// dmap(g, j) gives the head-dim index of accumulator row g of m-tile j.
-template <int WARPS, class DMap>
-QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, int kvh,
-                                float m0, float m1, float l0, float l1,
-                                const float (&o)[16][4], bool consumer, DMap dmap) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
-#pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    l0 += shfl_xor(l0, off);
-    l1 += shfl_xor(l1, off);
-  }
-  float* red = reinterpret_cast<float*>(smem);          // [WARPS][8][256]
-  float* mlred = red + WARPS * 8 * kHeadDim;              // [WARPS][8][2]
-  if (consumer) {
-    float* ow = red + warp * 8 * kHeadDim;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int d = dmap(g, j);
-      *reinterpret_cast<float2*>(ow + (2 * qd) * kHeadDim + d) = make_float2(o[j][0], o[j][2]);
-      *reinterpret_cast<float2*>(ow + (2 * qd + 1) * kHeadDim + d) = make_float2(o[j][1], o[j][3]);
-    }
-    if (g == 0) {
-      mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
-      mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
-      mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
-      mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
-    }
-  }
-  __syncthreads();
-  for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
-    const int col = idx >> 8, d = idx & 255;
-    float M = -CUDART_INF_F;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, mlred[(w * 8 + col) * 2]);
-    float acc = 0.f, ls = 0.f;
-#pragma unroll
-    for (int w = 0; w < WARPS; ++w) {
-      const float mw = mlred[(w * 8 + col) * 2];
-      const float wt = (mw == -CUDART_INF_F) ? 0.f : exp2_approx(mw - M);
-      acc += wt * red[(w * 8 + col) * kHeadDim + d];
-      ls += wt * mlred[(w * 8 + col) * 2 + 1];
-    }
-    const size_t R = (size_t)(kvh * kGroup + col);
-    const size_t base = R * p.num_splits + split;
-    p.partial_o[base * kHeadDim + d] = acc;
-    if (d == 0) {
-      p.partial_ml[base * 2 + 0] = M;
-      p.partial_ml[base * 2 + 1] = ls;
-    }
-  }
-}
-
-}  // namespace
-
-// =====================================================================
-// NVFP4 decode, q_len = 1.
-// =====================================================================
-// Warp WARPS is the producer: its lane 0 streams 64-token stages of one KV
-// head (codes and scales of K and V, four TMA boxes, 18 KB) into an
-// NST-deep ring guarded by full/empty mbarriers.  Warps 0..WARPS-1 consume:
-// warp w owns tokens 16w..16w+15 of every stage.  No CTA-wide barrier runs
-// inside the loop.
-template <typename T, int WARPS, int NST>
-__global__ void __launch_bounds__((WARPS + 1) * 32, 2)
-    nvfp4_decode_kernel(const __grid_constant__ SplitParams p) {
-  constexpr int ST = WARPS * 16;
-  constexpr int CODE_TILE = ST * kCodeBytes;
-  constexpr int SCALE_TILE = ST * kScaleBytes;
-  constexpr int STAGE_BYTES = 2 * CODE_TILE + 2 * SCALE_TILE;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  // TMA boxes with the 128-byte swizzle need 1024-byte aligned destinations
-  const uint32_t sbase = (smem_u32(smem) + 1023u) & ~1023u;
-  const uint32_t bar_full = sbase + NST * STAGE_BYTES;
-  const uint32_t bar_empty = bar_full + 8 * NST;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y;
-
-  const StageRange rg = stage_range<ST>(p, split);
-
-  if (tid == 0) {
-#pragma unroll
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, WARPS);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-
-  float o[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
-  const bool consumer = warp < WARPS;
-
-  if (!consumer) {
-    if (lane == 0 && rg.n_st > 0) {
-      tma_prefetch_desc(&p.tm_kc);
-      tma_prefetch_desc(&p.tm_vc);
-      tma_prefetch_desc(&p.tm_ks);
-      tma_prefetch_desc(&p.tm_vs);
-      int issued = 0;
-      for (int k = 0; k < rg.n_st; ++k) {
-        const int slot = k % NST;
-        if (k >= NST && !mbar_wait(bar_empty + 8 * slot, ((k / NST) - 1) & 1)) {
-          flag_error(kErrTimeout);
-          break;
-        }
-        const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
-        const int pp = lookup_page(p, t0, true);
-        const uint32_t fb = bar_full + 8 * slot, dst = sbase + slot * STAGE_BYTES;
-        ++issued;
-        if (pp < 0) {  // bad page id: no copy; consumers mask the whole stage
-          mbar_arrive(fb);
-          continue;
-        }
-        mbar_arrive_expect_tx(fb, STAGE_BYTES);
-        const int y = pp * kPage + (t0 & (kPage - 1));
-        tma_load_2d(dst, &p.tm_kc, kvh * kCodeBytes, y, fb);
-        tma_load_2d(dst + CODE_TILE, &p.tm_vc, kvh * kCodeBytes, y, fb);
-        tma_load_2d(dst + 2 * CODE_TILE, &p.tm_ks, kvh * kScaleBytes, y, fb);
-        tma_load_2d(dst + 2 * CODE_TILE + SCALE_TILE, &p.tm_vs, kvh * kScaleBytes, y, fb);
-      }
-      // never leave with copies in flight (only matters after a timeout)
-      for (int k = max(0, issued - NST); k < issued; ++k)
-        if (!mbar_wait(bar_full + 8 * (k % NST), (k / NST) & 1)) flag_error(kErrTimeout);
-    }
-  }
-
-  uint32_t qf[32];
-  float cf0 = 0.f, cf1 = 0.f;
-  if (consumer)
-    load_q_decode<T>(reinterpret_cast<const T*>(p.q), g < kGroup ? kvh * kGroup + g : -1, qd,
-                     p.sm_scale_log2, qf, cf0, cf1);
-
-  for (int k = 0; consumer && k < rg.n_st; ++k) {
-    const int slot_i = k % NST;
-    if (!mbar_wait(bar_full + 8 * slot_i, (k / NST) & 1)) {
-      flag_error(kErrTimeout);
-      break;
-    }
-    const uint32_t slot = sbase + slot_i * STAGE_BYTES;
-    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
-    const int valid_end = lookup_page(p, t0, false) >= 0 ? rg.tok_end : t0;
-    const int tw0 = t0 + 16 * warp;
-
-    // ---------------- S^T = K Q^T over the 16 tokens of this warp
-    const int r0 = 16 * warp + g, r1 = r0 + 8;
-    uint32_t kw0[8], kw1[8];
-    {
-      const uint4 a = lds128(slot + swz128(r0, 2 * qd));
-      const uint4 b = lds128(slot + swz128(r0, 2 * qd + 1));
-      const uint4 c = lds128(slot + swz128(r1, 2 * qd));
-      const uint4 d = lds128(slot + swz128(r1, 2 * qd + 1));
-      kw0[0] = a.x; kw0[1] = a.y; kw0[2] = a.z; kw0[3] = a.w;
-      kw0[4] = b.x; kw0[5] = b.y; kw0[6] = b.z; kw0[7] = b.w;
-      kw1[0] = c.x; kw1[1] = c.y; kw1[2] = c.z; kw1[3] = c.w;
-      kw1[4] = d.x; kw1[5] = d.y; kw1[6] = d.z; kw1[7] = d.w;
-    }
-    uint32_t sc0[4], sc1[4];
-    scales_bcast4(lds32(slot + 2 * CODE_TILE + r0 * 16 + 4 * qd), sc0);
-    scales_bcast4(lds32(slot + 2 * CODE_TILE + r1 * 16 + 4 * qd), sc1);
-
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) {
-      uint32_t h0[4], h1[4];
-      e2m1x8_to_f16x2x4(kw0[w8], h0);
-      e2m1x8_to_f16x2x4(kw1[w8], h1);
-      const uint32_t s0 = sc0[w8 >> 1], s1 = sc1[w8 >> 1];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        h0[j] = hmul2_u32(h0[j], s0);
-        h1[j] = hmul2_u32(h1[j], s1);
-      }
-      mma_16816(sa, h0[0], h1[0], h0[1], h1[1], qf[4 * w8 + 0], qf[4 * w8 + 1]);
-      mma_16816(sb, h0[2], h1[2], h0[3], h1[3], qf[4 * w8 + 2], qf[4 * w8 + 3]);
-    }
-    float t[4] = {(sa[0] + sb[0]) * cf0, (sa[1] + sb[1]) * cf1, (sa[2] + sb[2]) * cf0,
-                  (sa[3] + sb[3]) * cf1};
-    const bool tail = tw0 + 16 > valid_end;
-    if (tail) {
-      if (tw0 + g >= valid_end) t[0] = t[1] = -CUDART_INF_F;
-      if (tw0 + g + 8 >= valid_end) t[2] = t[3] = -CUDART_INF_F;
-    }
-    const PFrag pf = softmax_step_decode(t, m0, m1, l0, l1, o);
-
-    // ---------------- O^T += V^T P^T
-    const int ra = 16 * warp + 2 * qd;
-    const uint32_t vbase = slot + CODE_TILE;
-    const uint4 va = lds128(vbase + swz128(ra, g));
-    const uint4 vb = lds128(vbase + swz128(ra + 1, g));
-    const uint4 vcc = lds128(vbase + swz128(ra + 8, g));
-    const uint4 vd = lds128(vbase + swz128(ra + 9, g));
-    const uint32_t vsb = slot + 2 * CODE_TILE + SCALE_TILE + 2 * g;
-    uint32_t sa16 = lds16(vsb + ra * 16), sb16 = lds16(vsb + (ra + 1) * 16);
-    uint32_t sc16 = lds16(vsb + (ra + 8) * 16), sd16 = lds16(vsb + (ra + 9) * 16);
-    if (tail) {  // rows past the valid end hold stale bytes: zero their scales
-      const int ta = t0 + ra;
-      if (ta >= valid_end) sa16 = 0;
-      if (ta + 1 >= valid_end) sb16 = 0;
-      if (ta + 8 >= valid_end) sc16 = 0;
-      if (ta + 9 >= valid_end) sd16 = 0;
-    }
-    uint32_t spab0, spab1, spcd0, spcd1;
-    e4m3x4_to_f16x2x2(__byte_perm(sa16, sb16, 0x5140), spab0, spab1);
-    e4m3x4_to_f16x2x2(__byte_perm(sc16, sd16, 0x5140), spcd0, spcd1);
-    const uint32_t VA[4] = {va.x, va.y, va.z, va.w};
-    const uint32_t VB[4] = {vb.x, vb.y, vb.z, vb.w};
-    const uint32_t VC[4] = {vcc.x, vcc.y, vcc.z, vcc.w};
-    const uint32_t VD[4] = {vd.x, vd.y, vd.z, vd.w};
-#pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) {
-      const uint32_t xab = (VA[w4] & 0x0F0F0F0Fu) | ((VB[w4] << 4) & 0xF0F0F0F0u);
-      const uint32_t yab = ((VA[w4] >> 4) & 0x0F0F0F0Fu) | (VB[w4] & 0xF0F0F0F0u);
-      const uint32_t xcd = (VC[w4] & 0x0F0F0F0Fu) | ((VD[w4] << 4) & 0xF0F0F0F0u);
-      const uint32_t ycd = ((VC[w4] >> 4) & 0x0F0F0F0Fu) | (VD[w4] & 0xF0F0F0F0u);
-      uint32_t hxab[4], hyab[4], hxcd[4], hycd[4];
-      e2m1x8_to_f16x2x4(xab, hxab);
-      e2m1x8_to_f16x2x4(yab, hyab);
-      e2m1x8_to_f16x2x4(xcd, hxcd);
-      e2m1x8_to_f16x2x4(ycd, hycd);
-      const uint32_t sab = w4 < 2 ? spab0 : spab1;
-      const uint32_t scd = w4 < 2 ? spcd0 : spcd1;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t a0 = hmul2_u32(hxab[kk], sab), a1 = hmul2_u32(hyab[kk], sab);
-        const uint32_t a2 = hmul2_u32(hxcd[kk], scd), a3 = hmul2_u32(hycd[kk], scd);
-        mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.hi0, pf.hi1);
-        mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.lo0, pf.lo1);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bar_empty + 8 * slot_i);
-  }
-
-  __syncthreads();
-  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, consumer,
-                         [](int gg, int j) { return 32 * gg + 2 * j; });
-}
+using namespace detail;
 
 // =====================================================================
 // NVFP4 verify, q_len 2..8 (rows = 6 * q_len <= 8 * NT).
@@ -969,21 +554,6 @@ cudaError_t set_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-template <typename T>
-cudaError_t launch_decode(const SplitParams& p, cudaStream_t stream) {
-  constexpr int WARPS = 4, NST = 6;
-  constexpr int ST = WARPS * 16;
-  const int stage = 2 * ST * kCodeBytes + 2 * ST * kScaleBytes;
-  const int epi = WARPS * 8 * kHeadDim * 4 + WARPS * 16 * 4;
-  const int bytes = max(NST * stage + 16 * NST, epi) + 1024;
-  auto kernel = nvfp4_decode_kernel<T, WARPS, NST>;
-  cudaError_t e = set_smem(kernel, bytes);
-  if (e != cudaSuccess) return e;
-  dim3 grid(p.num_splits, kKvHeads);
-  kernel<<<grid, (WARPS + 1) * 32, bytes, stream>>>(p);
-  return cudaGetLastError();
-}
-
 template <typename T, int NT>
 cudaError_t launch_verify_nt(const SplitParams& p, cudaStream_t stream) {
   constexpr int NST = 3, ST = 64, NCOL = 8 * NT, WARPS = 4;
@@ -1015,8 +585,8 @@ cudaError_t launch_verify(const SplitParams& p, cudaStream_t stream) {
 
 cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream) {
   if (p.q_len == 1) {
-    return dtype == kDtypeBF16 ? launch_decode<__nv_bfloat16>(p, stream)
-                               : launch_decode<__half>(p, stream);
+    return dtype == kDtypeBF16 ? launch_nvfp4_decode<__nv_bfloat16>(p, stream)
+                               : launch_nvfp4_decode<__half>(p, stream);
   }
   return dtype == kDtypeBF16 ? launch_verify<__nv_bfloat16>(p, stream)
                              : launch_verify<__half>(p, stream);

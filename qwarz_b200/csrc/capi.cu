@@ -90,17 +90,18 @@ int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t row
   return QWZ_OK;
 }
 
-// Descriptors of the NVFP4 pool: codes [P*256, 512 B] (128 x 64 boxes,
-// 128-byte swizzle), scales [P*256, 64 B] (16 x 64 boxes).
+// Descriptors of the NVFP4 pool: codes [P*256, 512 B] (boxes of one head's
+// 128 B x one 256-token page, 128-byte swizzle), scales [P*256, 64 B]
+// (16 B x 256 boxes).
 int encode_pool(qwz::SplitParams& p, int32_t num_pages) {
   const uint64_t rows = (uint64_t)num_pages * qwz::kPage;
-  int rc = encode_2d(&p.tm_kc, p.k_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64,
+  int rc = encode_2d(&p.tm_kc, p.k_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, qwz::kPage,
                      CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_2d(&p.tm_vc, p.v_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64,
+  if (!rc) rc = encode_2d(&p.tm_vc, p.v_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, qwz::kPage,
                           CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_2d(&p.tm_ks, p.k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64,
+  if (!rc) rc = encode_2d(&p.tm_ks, p.k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, qwz::kPage,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!rc) rc = encode_2d(&p.tm_vs, p.v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64,
+  if (!rc) rc = encode_2d(&p.tm_vs, p.v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, qwz::kPage,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
   return rc;
 }

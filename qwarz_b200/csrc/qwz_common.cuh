@@ -206,6 +206,11 @@ QWZ_DEVINL void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
+// Orders this thread's earlier shared-memory accesses (generic proxy) before
+// its later TMA writes into the same bytes (async proxy).
+QWZ_DEVINL void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
 QWZ_DEVINL void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
