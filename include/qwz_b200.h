@@ -39,6 +39,7 @@ extern "C" {
 #define QWZ_DEVERR_TABLE_RANGE 1
 #define QWZ_DEVERR_PAGE_RANGE 2
 #define QWZ_DEVERR_SLOT_RANGE 4
+#define QWZ_DEVERR_TIMEOUT 8 /* a bounded in-kernel wait gave up */
 
 /* Library version string. */
 const char* qwz_version(void);
@@ -128,6 +129,25 @@ int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache,
                      const int32_t* cache_seqlens, void* out, float* partial_o,
                      float* partial_ml, int32_t table_width, int32_t num_pages, int32_t q_len,
                      int32_t num_splits, float sm_scale, int32_t dtype, void* stream);
+
+/*
+ * qwz_nvfp4_attend without a caller-supplied workspace.  No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory
+ * (an engine that owns every allocation, a fixed memory pool, an FFI that
+ * only passes raw input/output pointers).  The split-K partials live in a
+ * static device array of 4096 (query row x split) records, 4 MiB + 32 KiB,
+ * held by every GPU that loads the library until the process exits.
+ * Requests with q_len * 24 * num_splits > 4096 return QWZ_EINVAL.  The first
+ * call on a device resolves the array's device address (cudaGetSymbolAddress
+ * with that device current) and must come before any stream capture on it.
+ * Calls share the array and race if they overlap on the GPU: serialise them.
+ * Allocates nothing; arguments otherwise as qwz_nvfp4_attend.
+ */
+int qwz_nvfp4_attend_noalloc(const void* q, const void* k, const void* v, void* k_cache,
+                             void* v_cache, void* k_scales, void* v_scales,
+                             const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                             int32_t table_width, int32_t num_pages, int32_t q_len,
+                             int32_t num_splits, float sm_scale, int32_t dtype, void* stream);
 
 /*
  * Sequence-sharded decode, local half: attention of q over the logical

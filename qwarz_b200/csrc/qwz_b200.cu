@@ -5,3 +5,4 @@
 #include "attn_combine.cu"
 #include "kv_write.cu"
 #include "capi.cu"
+#include "noalloc.cu"
