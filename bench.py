@@ -1,7 +1,7 @@
 """Benchmark of the NVFP4-KV decode attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c2|c3_32k|c3_131k|c4|c5]
+                    [--workload auto|c3|c4|c5|all]
 
 Default workload ("auto"): one decode step = q_len 1 attention over 16
 attention layers, each with independent seeded NVFP4 KV of 65,536 tokens per
@@ -62,7 +62,7 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML every 100 ms."""
+    """Samples SM clock and throttle reasons through NVML every 10 ms."""
 
     REASONS = {
         "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
@@ -93,7 +93,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            self._stop.wait(0.1)
+            self._stop.wait(0.01)
 
     def __enter__(self):
         if self.nvml is not None:
@@ -268,7 +268,6 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
     split_ms_launch = t_split_ms / args.steps / LAYERS
 
     # ----- end to end through the public API, host copies inside the graph
-    e2e_ms = None
     h2d = LAYERS * (q[0].numel() + knew[0].numel() + vnew[0].numel()) * 2
     d2h = LAYERS * out[0].numel() * 2
     if world == 1:
@@ -291,19 +290,38 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
                 host_o[l].copy_(res, non_blocking=True)
 
         qattn.release_attention_plans()
-        e2e_graph = capture(e2e_step)
-        for _ in range(args.warmup):
-            e2e_graph.replay()
-        torch.cuda.synchronize()
-        e2e_ms = cuda_time(e2e_graph.replay, args.steps, torch.cuda.current_stream(device)) / args.steps
-        del e2e_graph
+    else:
+        host_q = [t.cpu().pin_memory() for t in q]
+        host_k = [t.cpu().pin_memory() for t in knew]
+        host_v = [t.cpu().pin_memory() for t in vnew]
+        host_o = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in out]
+        dq = [torch.empty_like(t) for t in q]
+        dk = [torch.empty_like(t) for t in knew]
+        dv = [torch.empty_like(t) for t in vnew]
+
+        def e2e_step():
+            for l in range(LAYERS):
+                dq[l].copy_(host_q[l], non_blocking=True)
+                dk[l].copy_(host_k[l], non_blocking=True)
+                dv[l].copy_(host_v[l], non_blocking=True)
+                cache, perm = layers[l]
+                res = dec.step(dq[l], dk[l], dv[l], cache, perm, pre, out[l])
+                host_o[l].copy_(res, non_blocking=True)
+
+    e2e_graph = capture(e2e_step)
+    for _ in range(args.warmup):
+        e2e_graph.replay()
+    barrier()
+    e2e_ms = cuda_time(e2e_graph.replay, args.steps, torch.cuda.current_stream(device)) / args.steps
+    barrier()
+    del e2e_graph
 
     # ----- aggregate over ranks
     bytes_rank = LAYERS * layer_bytes(local_tokens, 1, local_pages)
     if world > 1:
-        t = torch.tensor([ms_step, split_ms_launch], dtype=torch.float64, device=device)
+        t = torch.tensor([ms_step, split_ms_launch, e2e_ms], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_step, split_ms_launch = float(t[0]), float(t[1])
+        ms_step, split_ms_launch, e2e_ms = float(t[0]), float(t[1]), float(t[2])
     del graph, split_graph
     if rank != 0:
         return None
@@ -363,15 +381,161 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
             "us_per_step": e2e_ms * 1e3,
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": "qwarz_b200.attention.attend per layer, pinned H2D/D2H, captured in one CUDA graph",
+            "api": ("qwarz_b200.attention.attend per layer" if world == 1 else
+                    "qwarz_b200.sharded.ShardedDecode.step per layer (NCCL all-gather inside)")
+                   + ", pinned H2D/D2H, captured in one CUDA graph, max over ranks",
         },
-        "gpu_launches": args.steps * LAYERS * 3 + args.steps * LAYERS,
+        # our kernels per timed step: append, split, combine (+ shard combine at N>1),
+        # plus the split-only roofline graph
+        "gpu_launches": args.steps * LAYERS * (3 if world == 1 else 4) + args.steps * LAYERS,
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
         sample = cpu_layers_for_oracle(layers, [t.view(1, HEADS, DIM) for t in q], 2)
         result["cpu_baseline"] = cpu_oracle_sample(sample, local_tokens, args.cpu_seconds)
     return result
+
+
+# ------------------------------------------------- other BASELINE configs
+def graph_time_ms(fn, warmup: int, steps: int, stream) -> float:
+    for _ in range(max(3, warmup)):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ms = cuda_time(graph.replay, steps, stream) / steps
+    del graph
+    return ms
+
+
+def run_extra(args, device) -> dict:
+    """C3 (MTP7 verify at 32K and 131K), C4 (262K on one GPU) and C5 (FP8
+    draft, 6 steps in one CUDA graph); one JSON object with per-config
+    device times and HBM fractions (not the driver's headline line)."""
+    from qwarz_b200 import build, ops
+    from qwarz_b200.draft_attention import DecodeAttention, shadow_write
+
+    build.build()
+    stream = torch.cuda.current_stream(device)
+    pk, pk_kind = peaks()
+    res = {"workload": args.workload, "peak_gbs": pk["hbm_gbs"], "peak_kind": pk_kind, "configs": {}}
+    g = torch.Generator(device=device).manual_seed(7)
+    dtype = torch.bfloat16
+
+    def nvfp4_config(tokens, q_len, layers):
+        pages = tokens // PAGE
+        lay = [build_layer(ops, device, pages, tokens, seed=3000 + l) for l in range(layers)]
+        q = [torch.randn(q_len, HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(layers)]
+        kn = [torch.randn(q_len, KV_HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(layers)]
+        vn = [torch.randn(q_len, KV_HEADS, DIM, generator=g, device=device).to(dtype) for _ in range(layers)]
+        out = [torch.empty_like(t) for t in q]
+        pre = torch.tensor([tokens - q_len], dtype=torch.int32, device=device)
+        splits = ops.default_splits(device, tokens, q_len)
+        po, pml = ops.split_workspace(device, q_len, splits)
+
+        def step():
+            for l in range(layers):
+                c, perm = lay[l]
+                ops.nvfp4_attend(q[l], kn[l], vn[l], *c, perm, pre, out[l], po, pml, splits)
+
+        def split_only():
+            for l in range(layers):
+                c, perm = lay[l]
+                ops.attn_split(q[l], c[0], c[1], perm, pre, po, pml, c[2], c[3], splits)
+
+        ms = graph_time_ms(step, args.warmup, args.steps, stream)
+        ms_split = graph_time_ms(split_only, args.warmup, args.steps, stream) / layers
+        byt = layer_bytes(tokens, q_len, pages)
+        del lay
+        torch.cuda.empty_cache()
+        return {"tokens": tokens, "q_len": q_len, "layers": layers, "splits": splits,
+                "us_per_step": ms * 1e3, "us_per_layer_call": ms * 1e3 / layers,
+                "split_us_per_launch": ms_split * 1e3,
+                "split_GBps": byt / (ms_split * 1e-3) / 1e9,
+                "split_frac": byt / (ms_split * 1e-3) / 1e9 / pk["hbm_gbs"],
+                "step_GBps": layers * byt / (ms * 1e-3) / 1e9,
+                "verify_flops_per_layer": 4 * 256 * 24 * (q_len * (tokens - q_len) + q_len * (q_len + 1) // 2)}
+
+    if args.workload in ("c3", "all"):
+        for tokens in (32768, 131072):
+            v7 = nvfp4_config(tokens, 7, 16)
+            d1 = nvfp4_config(tokens, 1, 16)
+            v7["tensor_TFLOPs_split"] = v7["verify_flops_per_layer"] / (v7["split_us_per_launch"] * 1e-6) / 1e12
+            res["configs"][f"c3_{tokens}"] = {"verify_q7": v7, "decode_q1": d1,
+                                              "verify_over_decode_step": v7["us_per_step"] / d1["us_per_step"]}
+    if args.workload in ("c4", "all"):
+        res["configs"]["c4_262144_1gpu"] = nvfp4_config(262144, 1, 16)
+    if args.workload in ("c5", "all"):
+        T = 65536 + 6
+        base = 65536
+        kf = torch.randn(T, KV_HEADS, DIM, generator=g, device=device)
+        vf = torch.randn(T, KV_HEADS, DIM, generator=g, device=device)
+        pages = (T + PAGE - 1) // PAGE
+        ksc = torch.full((pages, KV_HEADS), 0.02, dtype=torch.float32, device=device)
+        vsc = torch.full((pages, KV_HEADS), 0.03, dtype=torch.float32, device=device)
+        k8 = (kf / 0.02).clamp(-448, 448).to(torch.float8_e4m3fn)[None]
+        v8 = (vf / 0.03).clamp(-448, 448).to(torch.float8_e4m3fn)[None]
+        del kf, vf
+        attn = DecodeAttention(HEADS, KV_HEADS, DIM, device, splits=16)
+        qd = torch.randn(1, 1, HEADS, DIM, generator=g, device=device).half()
+        kn = torch.randn(6, KV_HEADS, DIM, generator=g, device=device).half()
+        vn = torch.randn(6, KV_HEADS, DIM, generator=g, device=device).half()
+        outd = torch.empty_like(qd)
+        pos = [torch.tensor([base + i], dtype=torch.int32, device=device) for i in range(6)]
+        lens = [torch.tensor([base + i + 1], dtype=torch.int32, device=device) for i in range(6)]
+
+        def roll():
+            for i in range(6):
+                shadow_write(kn[i], vn[i], k8[0], v8[0], pos[i], ksc, vsc)
+                attn.attend(qd, k8, v8, lens[i], outd, ksc, vsc)
+
+        ms = graph_time_ms(roll, args.warmup, args.steps, stream)
+        step_bytes = 2 * 4 * 256 * (base + 3) + 2 * 4 * 4 * pages + 2 * 24 * 256 * 2 + 2 * 4 * 256 * 3
+        res["configs"]["c5_draft_fp8"] = {
+            "tokens": base, "steps_per_graph": 6, "splits": 16, "us_per_graph": ms * 1e3,
+            "us_per_step": ms * 1e3 / 6, "GBps": 6 * step_bytes / (ms * 1e-3) / 1e9,
+            "frac": 6 * step_bytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+    return res
+
+
+def run_profile_case(args, device) -> dict:
+    """Small case for ncu --set full: one 65,536-token layer (75.5 MB, above
+    the L2 working set only with ncu's cache flush between passes), three
+    eager launches of the decode split, the q_len 7 verify split, or the FP8
+    draft decode."""
+    from qwarz_b200 import build, ops
+    from qwarz_b200.draft_attention import DecodeAttention
+
+    build.build()
+    tokens, pages = 65536, 256
+    g = torch.Generator(device=device).manual_seed(11)
+    if args.workload == "profile_draft":
+        T = tokens + 6
+        k8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
+        v8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
+        q = torch.randn(1, 1, HEADS, DIM, generator=g, device=device).half()
+        out = torch.empty_like(q)
+        attn = DecodeAttention(HEADS, KV_HEADS, DIM, device)
+        length = torch.tensor([tokens], dtype=torch.int32, device=device)
+        for _ in range(3):
+            attn.attend(q, k8, v8, length, out)
+    else:
+        q_len = 7 if args.workload == "profile_verify" else 1
+        cache, perm = build_layer(ops, device, pages, tokens, seed=1)
+        q = torch.randn(q_len, HEADS, DIM, generator=g, device=device).bfloat16()
+        pre = torch.tensor([tokens - q_len], dtype=torch.int32, device=device)
+        splits = ops.default_splits(device, tokens, q_len)
+        po, pml = ops.split_workspace(device, q_len, splits)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.attn_split(q, cache[0], cache[1], perm, pre, po, pml, cache[2], cache[3], splits)
+            ops.attn_combine(po, pml, out, splits)
+    torch.cuda.synchronize()
+    return {"workload": args.workload, "tokens": tokens, "ok": True}
 
 
 # --------------------------------------------------------- reference arm
@@ -443,11 +607,18 @@ def run_reference(args) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "c3", "c4", "c5", "all", "profile_decode", "profile_verify",
+                             "profile_draft"],
+                    help="auto: the driver's headline (C2 at N=1, weak-scaled sharding at N>1); "
+                         "c3/c4/c5/all: the other BASELINE configs on one GPU (separate JSON); "
+                         "profile_*: three eager launches of one kernel on one 65,536-token layer, "
+                         "the small case for ncu --set full")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -461,6 +632,12 @@ def main():
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.workload.startswith("profile_"):
+        print(json.dumps(run_profile_case(args, device)), flush=True)
+        return
+    if args.workload != "auto":
+        print(json.dumps(run_extra(args, device)), flush=True)
+        return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)

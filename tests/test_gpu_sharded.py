@@ -1,0 +1,74 @@
+"""Sequence-sharded decode on one GPU: G shards, each with its own NVFP4 pool
+and local block table, reduced to (m, l, O) records by qwz_attn_shard_partial
+and merged by qwz_lse_combine_gathered, against the FP32 oracle over the whole
+sequence.  (The NCCL exchange between real ranks is the same buffer layout;
+its host logic is tested on gloo ranks in test_host.py.)"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import rng
+from qwarz_b200 import sharded
+from tests.conftest import assert_close_attention
+from tests.gpu_helpers import make_cache, queries, to_cpu_torch, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world,total", [(2, 2000), (4, 4096), (8, 4100), (3, 1500)])
+def test_sharded_records_combine_to_full_attention(cuda, world, total):
+    from qwarz_b200 import ops
+
+    pages = (total + 255) // 256 + (1 if world == 8 else 0)
+    pages = max(pages, world)
+    table = rng.permutation(31 + world, pages)
+    c, _, _ = make_cache(500 + world, total, pages, table)
+    full = to_cpu_torch(c)
+    q = queries(600 + world, 1)
+    ref = oatt.nvfp4_attention(q.float(), full["k_cache"], full["v_cache"], full["k_scales"],
+                               full["v_scales"], full["table"], total - 1)
+    shards = sharded.shard_pages(pages, world)
+    gathered = torch.empty(world, 24, 258, dtype=torch.float32, device=cuda)
+    lens = torch.tensor([total - 1], dtype=torch.int32, device=cuda)
+    qd = q.to(cuda)
+    for s in shards:
+        # the shard's own pool: its logical pages, physically renumbered 0..n-1
+        phys = table[s.first_page:s.first_page + s.num_pages]
+        local = {n: np.ascontiguousarray(c[n][phys]) for n in ("k_cache", "v_cache", "k_scales", "v_scales")}
+        local["table"] = np.arange(s.num_pages, dtype=np.int32)
+        dc = to_device(local, cuda)
+        splits = 3
+        po, pml = ops.split_workspace(cuda, 1, splits)
+        ops.shard_partial(qd, dc["k_cache"], dc["v_cache"], dc["k_scales"], dc["v_scales"],
+                          dc["table"], lens, po, pml, gathered[s.rank], s.tok_begin, s.tok_span, splits)
+    out = torch.empty(1, 24, 256, dtype=torch.float16, device=cuda)
+    ops.combine_gathered(gathered, out, world)
+    torch.cuda.synchronize()
+    assert_close_attention(out.float().cpu().numpy(), ref.numpy(), f"sharded world={world}")
+
+
+def test_shard_append_writes_only_the_owners_rows(cuda):
+    """Every shard launches the writer; only the owner of the position stores it."""
+    from qwarz_b200 import ops
+
+    world, pages = 2, 4
+    shards = sharded.shard_pages(pages, world)
+    pre = 2 * 256 + 5          # position owned by rank 1 (pages 2..3)
+    k = torch.randn(1, 4, 256, device=cuda).half()
+    v = torch.randn(1, 4, 256, device=cuda).half()
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    for s in shards:
+        cache = [torch.zeros(s.num_pages, 256, 4, 128, dtype=torch.uint8, device=cuda),
+                 torch.zeros(s.num_pages, 256, 4, 128, dtype=torch.uint8, device=cuda),
+                 torch.zeros(s.num_pages, 256, 4, 16, dtype=torch.uint8, device=cuda),
+                 torch.zeros(s.num_pages, 256, 4, 16, dtype=torch.uint8, device=cuda)]
+        table = torch.arange(s.num_pages, dtype=torch.int32, device=cuda)
+        ops.nvfp4_append_shard(k, v, *cache, table, lens, s.first_page)
+        torch.cuda.synchronize()
+        written = any(int(t.count_nonzero()) for t in cache)
+        assert written == (s.rank == sharded.owner(pre, shards)), s
+    from qwarz_b200 import _lib
+    assert _lib.device_error(clear=True) == 0
