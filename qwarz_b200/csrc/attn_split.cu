@@ -417,134 +417,6 @@ __global__ void __launch_bounds__(128, 2) nvfp4_verify_kernel(const SplitParams 
 }
 
 // =====================================================================
-// FP8 (E4M3) draft decode, q_len = 1, contiguous [T, 4, 256] K/V with an
-// optional FP32 scale per (256-token page, KV head).
-// =====================================================================
-QWZ_DEVINL uint32_t swz256(int row, int ch) {
-  return static_cast<uint32_t>(row * 256 + ((ch ^ (row & 7) ^ ((ch >> 3) << 1)) << 4));
-}
-
-template <int WARPS, int NST>
-__global__ void __launch_bounds__(WARPS * 32, 1) fp8_decode_kernel(const SplitParams p) {
-  constexpr int ST = WARPS * 16;
-  constexpr int TILE = ST * kHeadDim;  // one tensor, one head, ST tokens
-  constexpr int STAGE_BYTES = 2 * TILE;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  const uint32_t sbase = smem_u32(smem);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y;
-
-  const StageRange rg = stage_range<ST>(p, split);
-
-  uint32_t qf[32];
-  float cf0, cf1;
-  load_q_decode<__half>(reinterpret_cast<const __half*>(p.q),
-                        g < kGroup ? kvh * kGroup + g : -1, qd, p.sm_scale_log2, qf, cf0, cf1);
-
-  float o[16][4];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-  float m0 = -CUDART_INF_F, m1 = -CUDART_INF_F, l0 = 0.f, l1 = 0.f;
-
-  auto issue = [&](int k) {
-    const int t0 = p.tok_begin + (rg.st_lo + k) * ST;
-    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int idx = tid + (i & 7) * (WARPS * 32);
-      const int row = idx >> 4, ch = idx & 15;
-      const int t = t0 + row;
-      const bool ok = t < rg.tok_end && t < p.capacity;
-      const uint8_t* base = (i < 8) ? p.k_codes : p.v_codes;
-      const uint8_t* src = ok ? base + ((size_t)t * kKvHeads + kvh) * kHeadDim + ch * 16 : base;
-      cp_async16(slot + (i >> 3) * TILE + swz256(row, ch), src, ok ? 16u : 0u);
-    }
-  };
-
-#pragma unroll
-  for (int k = 0; k < NST - 1; ++k) {
-    if (k < rg.n_st) issue(k);
-    cp_async_commit();
-  }
-
-  for (int k = 0; k < rg.n_st; ++k) {
-    cp_async_wait<NST - 2>();
-    __syncthreads();
-    if (k + NST - 1 < rg.n_st) issue(k + NST - 1);
-    cp_async_commit();
-
-    const uint32_t slot = sbase + (k % NST) * STAGE_BYTES;
-    const int tw0 = p.tok_begin + (rg.st_lo + k) * ST + 16 * warp;
-    const int page = tw0 >> 8;
-    const float kscale = p.k_page_scale ? __ldg(p.k_page_scale + page * kKvHeads + kvh) : 1.f;
-    const float vscale = p.v_page_scale ? __ldg(p.v_page_scale + page * kKvHeads + kvh) : 1.f;
-
-    const int r0 = 16 * warp + g, r1 = r0 + 8;
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      const uint4 a = lds128(slot + swz256(r0, 4 * qd + c4));
-      const uint4 b = lds128(slot + swz256(r1, 4 * qd + c4));
-      const uint32_t A[4] = {a.x, a.y, a.z, a.w};
-      const uint32_t B[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const int ks = 4 * c4 + w;
-        uint32_t a0, a2, a1, a3;
-        e4m3x4_to_f16x2x2(A[w], a0, a2);
-        e4m3x4_to_f16x2x2(B[w], a1, a3);
-        if (w & 1)
-          mma_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
-        else
-          mma_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
-      }
-    }
-    const float f0 = cf0 * kscale, f1 = cf1 * kscale;
-    float t[4] = {(sa[0] + sb[0]) * f0, (sa[1] + sb[1]) * f1, (sa[2] + sb[2]) * f0,
-                  (sa[3] + sb[3]) * f1};
-    if (tw0 + 16 > rg.tok_end) {
-      if (tw0 + g >= rg.tok_end) t[0] = t[1] = -CUDART_INF_F;
-      if (tw0 + g + 8 >= rg.tok_end) t[2] = t[3] = -CUDART_INF_F;
-    }
-    PFrag pf = softmax_step_decode(t, m0, m1, l0, l1, o);
-    if (vscale != 1.f) pf = p_fragments(t[0] * vscale, t[1] * vscale, t[2] * vscale, t[3] * vscale);
-
-    const int ra = 16 * warp + 2 * qd;
-    const uint32_t vbase = slot + TILE;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int ch = g + 8 * half;
-      const uint4 va = lds128(vbase + swz256(ra, ch));
-      const uint4 vb = lds128(vbase + swz256(ra + 1, ch));
-      const uint4 vcc = lds128(vbase + swz256(ra + 8, ch));
-      const uint4 vd = lds128(vbase + swz256(ra + 9, ch));
-      const uint32_t VA[4] = {va.x, va.y, va.z, va.w};
-      const uint32_t VB[4] = {vb.x, vb.y, vb.z, vb.w};
-      const uint32_t VC[4] = {vcc.x, vcc.y, vcc.z, vcc.w};
-      const uint32_t VD[4] = {vd.x, vd.y, vd.z, vd.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-#pragma unroll
-        for (int pr = 0; pr < 2; ++pr) {
-          const uint32_t sel = pr ? 0x7362u : 0x5140u;
-          uint32_t a0, a1, a2, a3;
-          e4m3x4_to_f16x2x2(__byte_perm(VA[w], VB[w], sel), a0, a1);
-          e4m3x4_to_f16x2x2(__byte_perm(VC[w], VD[w], sel), a2, a3);
-          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.hi0, pf.hi1);
-          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.lo0, pf.lo1);
-        }
-      }
-    }
-  }
-
-  cp_async_wait<0>();
-  __syncthreads();
-  decode_epilogue<WARPS>(p, smem, split, kvh, m0, m1, l0, l1, o, true, [](int gg, int j) {
-    return j < 8 ? 16 * gg + 2 * j : 128 + 16 * gg + 2 * (j - 8);
-  });
-}
-
-// =====================================================================
 // launchers
 // =====================================================================
 namespace {
@@ -590,20 +462,6 @@ cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t str
   }
   return dtype == kDtypeBF16 ? launch_verify<__nv_bfloat16>(p, stream)
                              : launch_verify<__half>(p, stream);
-}
-
-cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream) {
-  constexpr int WARPS = 4, NST = 3;
-  constexpr int ST = WARPS * 16;
-  const int stage = 2 * ST * kHeadDim;
-  const int epi = WARPS * 8 * kHeadDim * 4 + WARPS * 16 * 4;
-  const int bytes = max(NST * stage, epi);
-  auto kernel = fp8_decode_kernel<WARPS, NST>;
-  cudaError_t e = set_smem(kernel, bytes);
-  if (e != cudaSuccess) return e;
-  dim3 grid(p.num_splits, kKvHeads);
-  kernel<<<grid, WARPS * 32, bytes, stream>>>(p);
-  return cudaGetLastError();
 }
 
 }  // namespace qwz

@@ -86,7 +86,7 @@ int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t row
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
                         box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(QWZ_EINVAL, "TMA descriptor encoding failed for the NVFP4 pool");
+  if (r != CUDA_SUCCESS) return fail(QWZ_EINVAL, "TMA descriptor encoding failed (base, stride or extent)");
   return QWZ_OK;
 }
 
@@ -384,7 +384,12 @@ int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const fl
   p.split_len = 0;
   p.num_splits = splits;
   p.sm_scale_log2 = (1.0f / 16.0f) * kLog2e;
-  int rc = launched(qwz::launch_fp8_split(p, as_stream(stream)), "qwz_fp8_draft_decode(split)");
+  // [capacity, 4 x 256 B] views; boxes of 128 head-dim bytes x 128 tokens.
+  const uint64_t row_bytes = (uint64_t)qwz::kKvHeads * qwz::kHeadDim;
+  int rc = encode_2d(&p.tm_kc, k8, row_bytes, (uint64_t)capacity, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_2d(&p.tm_vc, v8, row_bytes, (uint64_t)capacity, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = launched(qwz::launch_fp8_split(p, as_stream(stream)), "qwz_fp8_draft_decode(split)");
   if (rc) return rc;
   const qwz::CombineParams c = split_combine_params(part, stat, qwz::kQHeads, splits, out);
   return launched(qwz::launch_combine(c, qwz::kCombineFinal, QWZ_DTYPE_F16, as_stream(stream)),

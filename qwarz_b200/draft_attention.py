@@ -14,7 +14,7 @@ import torch
 
 from . import ops
 
-SPLITS = 16
+SPLITS = 37   # 37 splits x 4 KV heads = 148 CTAs, one per SM
 KV_HEADS = 4
 DIM = 256
 

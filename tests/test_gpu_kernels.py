@@ -274,6 +274,34 @@ def test_draft_with_page_scales_matches_oracle(cuda):
     assert_close_attention(out.float().cpu().view(1, 24, 256).numpy(), ref.numpy(), "draft scaled")
 
 
+@pytest.mark.parametrize("length", [1, 127, 128, 129, 383, 700])
+def test_draft_ignores_stale_rows_past_length(cuda, length):
+    """Rows at and past `length` hold E4M3 NaN bytes (0x7f): stages are read
+    whole, so the kernel must mask their scores and zero their values.  At
+    length == capacity the last stage runs past the store and reads the
+    copy engine's zero fill."""
+    from qwarz_b200.draft_attention import DecodeAttention
+
+    T = 700
+    k8 = nvfp4.fp8_shadow(cases.kv_rows(71, T))
+    v8 = nvfp4.fp8_shadow(cases.kv_rows(72, T))
+    k8[length:] = 0x7F
+    v8[length:] = 0x7F
+    kf = torch.from_numpy(nvfp4.e4m3_decode(k8[:length]))
+    vf = torch.from_numpy(nvfp4.e4m3_decode(v8[:length]))
+    q = queries(73, 1)
+    ref = oatt.attention_fp32(q.float(), kf, vf, 1 / 16, length - 1)
+    kd, vd = torch.from_numpy(k8).to(cuda)[None], torch.from_numpy(v8).to(cuda)[None]
+    lens = torch.tensor([length], dtype=torch.int32, device=cuda)
+    for splits in (1, 3, 37):
+        attn = DecodeAttention(24, 4, 256, cuda, splits=splits)
+        out = torch.empty(1, 1, 24, 256, dtype=torch.float16, device=cuda)
+        attn.attend(q.to(cuda).view(1, 1, 24, 256), kd, vd, lens, out)
+        torch.cuda.synchronize()
+        assert_close_attention(out.float().cpu().view(1, 24, 256).numpy(), ref.numpy(),
+                               f"draft stale length={length} splits={splits}")
+
+
 # ------------------------------------------------------------- diagnostics
 def test_bad_page_id_sets_device_error_without_fault(cuda):
     """A table entry outside the pool is skipped (zero-filled) and reported
