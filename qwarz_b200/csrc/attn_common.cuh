@@ -183,56 +183,70 @@ QWZ_DEVINL PFrag softmax_step_decode(float (&t)[4], float& m0, float& m1, float&
   return p_fragments(p0, p1, p2, p3);
 }
 
+// Shared-memory bytes of decode_epilogue for WARPS warps: per warp 16
+// m-tile rows of 32 lane float4s padded to 33 (writes conflict-free, reads
+// at most 2-way), then (m, l) per warp and column, then the merge weights.
+constexpr int kEpiRowF4 = 33;
+constexpr int epilogue_smem_bytes(int warps) {
+  return warps * 16 * kEpiRowF4 * 16 + warps * 8 * 2 * 4 + 8 * warps * 4;
+}
+
 // Cross-warp merge of decode-layout (m, l, O) and the partial store.
-// dmap(g, j) gives the head-dim index of accumulator row g of m-tile j.
-template <int WARPS, class DMap>
+// dinv(d, g, j) gives the lane row g and m-tile j whose accumulator row
+// holds head-dim d (the even member of the pair d, d+1 sits in c0/c1, the
+// odd one in c2/c3).  Summation order over warps is fixed.
+template <int WARPS, class DInv>
 QWZ_DEVINL void decode_epilogue(const SplitParams& p, uint8_t* smem, int split, int kvh,
                                 float m0, float m1, float l0, float l1,
-                                const float (&o)[16][4], bool consumer, DMap dmap) {
+                                const float (&o)[16][4], DInv dinv) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
     l0 += shfl_xor(l0, off);
     l1 += shfl_xor(l1, off);
   }
-  float* red = reinterpret_cast<float*>(smem);          // [WARPS][8][256]
-  float* mlred = red + WARPS * 8 * kHeadDim;              // [WARPS][8][2]
-  if (consumer) {
-    float* ow = red + warp * 8 * kHeadDim;
+  float4* red = reinterpret_cast<float4*>(smem);                       // [WARPS][16][33]
+  float* mlred = reinterpret_cast<float*>(red + WARPS * 16 * kEpiRowF4);  // [WARPS][8][2]
+  float* wts = mlred + WARPS * 16;                                      // [8 cols][WARPS]
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int d = dmap(g, j);
-      *reinterpret_cast<float2*>(ow + (2 * qd) * kHeadDim + d) = make_float2(o[j][0], o[j][2]);
-      *reinterpret_cast<float2*>(ow + (2 * qd + 1) * kHeadDim + d) = make_float2(o[j][1], o[j][3]);
-    }
-    if (g == 0) {
-      mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
-      mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
-      mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
-      mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
-    }
+  for (int j = 0; j < 16; ++j)
+    red[(warp * 16 + j) * kEpiRowF4 + lane] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+  if (g == 0) {
+    mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
+    mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
   }
   __syncthreads();
-  for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
-    const int col = idx >> 8, d = idx & 255;
+  if (tid < kGroup) {  // per column: CTA max, warp weights, l
+    const int col = tid;
     float M = -CUDART_INF_F;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) M = fmaxf(M, mlred[(w * 8 + col) * 2]);
-    float acc = 0.f, ls = 0.f;
+    float ls = 0.f;
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) {
       const float mw = mlred[(w * 8 + col) * 2];
       const float wt = (mw == -CUDART_INF_F) ? 0.f : exp2_approx(mw - M);
-      acc += wt * red[(w * 8 + col) * kHeadDim + d];
+      wts[col * WARPS + w] = wt;
       ls += wt * mlred[(w * 8 + col) * 2 + 1];
     }
-    const size_t R = (size_t)(kvh * kGroup + col);
-    const size_t base = R * p.num_splits + split;
+    const size_t base = (size_t)(kvh * kGroup + col) * p.num_splits + split;
+    p.partial_ml[base * 2 + 0] = M;
+    p.partial_ml[base * 2 + 1] = ls;
+  }
+  __syncthreads();
+  const float* rf = reinterpret_cast<const float*>(red);
+  for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
+    const int col = idx >> 8, d = idx & 255;
+    int gg, j;
+    dinv(d, gg, j);
+    const int src = ((j * kEpiRowF4) + 4 * gg + (col >> 1)) * 4 + (col & 1) + 2 * (d & 1);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) acc += wts[col * WARPS + w] * rf[w * 16 * kEpiRowF4 * 4 + src];
+    const size_t base = (size_t)(kvh * kGroup + col) * p.num_splits + split;
     p.partial_o[base * kHeadDim + d] = acc;
-    if (d == 0) {
-      p.partial_ml[base * 2 + 0] = M;
-      p.partial_ml[base * 2 + 1] = ls;
-    }
   }
 }
 

@@ -10,8 +10,10 @@
 // in a 3-deep ring; a full mbarrier per slot tracks the bytes.  There is no
 // producer warp: thread 0 issues the first three pages, and afterwards the
 // last warp to release a slot (a shared-memory counter) issues the next page
-// into it, so no warp ever waits for a slot to drain.  The CTA's physical
-// page ids are staged in shared memory up front (up to kDecPidCache pages).
+// into it, so no warp ever waits for a slot to drain.  The block-table row
+// (up to kDecPidCache entries) is staged in shared memory up front, loaded
+// in parallel with the sequence length.  (Measured on B200: separate K/V
+// barriers per slot, or issuing page 0 ahead of pages 1-2, do not pay.)
 // Warp w owns tokens 32w..32w+31 of every page as two independent 16-token
 // MMA tiles (A: +0..15, B: +16..31), which gives each warp two dependency
 // chains to interleave and one softmax update per 32 tokens.  Layout per
@@ -35,7 +37,8 @@ constexpr int kDecPidCache = 1024;                             // page ids stage
 constexpr int kDecCodeTile = kPage * kCodeBytes;               // 32 KB
 constexpr int kDecScaleTile = kPage * kScaleBytes;             // 4 KB
 constexpr int kDecStageBytes = 2 * kDecCodeTile + 2 * kDecScaleTile;
-// ring | full barriers | per-slot release counters, last issued page | page ids
+// ring | full barriers | per-slot release counters, page ends, last issued
+// page | table row
 constexpr int kDecMetaBytes = 8 * kDecStages + 16 * kDecStages;
 constexpr int kDecSmemBytes = kDecStages * kDecStageBytes + kDecMetaBytes + 4 * kDecPidCache + 1024;
 
@@ -142,10 +145,18 @@ struct DecMeta {
   int last_issued[kDecStages];  // CTA page index last issued into the slot
 };
 
-// Physical page of the CTA's k-th page (-1 when the id is bad).
+// Physical page of the CTA's k-th page (-1 when the id is bad).  pid[]
+// holds the first min(table_width, kDecPidCache) entries of the table row.
 QWZ_DEVINL int cta_page(const SplitParams& p, const int* pid, const StageRange& rg, int k) {
-  if (k < kDecPidCache) return pid[k];
-  return lookup_page(p, p.tok_begin + (rg.st_lo + k) * kPage, true);
+  const int t = p.tok_begin + (rg.st_lo + k) * kPage;
+  const int lp = (t >> 8) - p.table_page_offset;
+  if (lp < 0 || lp >= min(p.table_width, kDecPidCache)) return lookup_page(p, t, true);
+  const int pp = pid[lp];
+  if (pp < 0 || pp >= p.num_pages) {
+    flag_error(kErrPageRange);
+    return -1;
+  }
+  return pp;
 }
 
 // TMA of the CTA's k-th page into ring slot `slot` (one thread).
@@ -185,10 +196,21 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y;
 
+  // the table row is loaded while the length is in flight
+  constexpr int kRowPerThread = kDecPidCache / (kDecWarps * 32);
+  const int n_cached = min(p.table_width, kDecPidCache);
+  int row[kRowPerThread];
+#pragma unroll
+  for (int r = 0; r < kRowPerThread; ++r) {
+    const int i = tid + r * kDecWarps * 32;
+    row[r] = i < n_cached ? __ldg(p.block_table + i) : -1;
+  }
   const StageRange rg = stage_range<kPage>(p, split);
-
-  for (int i = tid; i < min(rg.n_st, kDecPidCache); i += blockDim.x)
-    pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
+#pragma unroll
+  for (int r = 0; r < kRowPerThread; ++r) {
+    const int i = tid + r * kDecWarps * 32;
+    if (i < n_cached) pid[i] = row[r];
+  }
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kDecStages; ++s) {
@@ -320,14 +342,15 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
     }
   }
   __syncthreads();
-  decode_epilogue<kDecWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, true,
-                             [](int gg, int j) { return 32 * gg + 2 * j; });
+  decode_epilogue<kDecWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int d, int& gg, int& j) {
+    gg = d >> 5;
+    j = (d & 31) >> 1;
+  });
 }
 
 template <typename T>
 cudaError_t launch_nvfp4_decode(const SplitParams& p, cudaStream_t stream) {
-  static_assert(kDecWarps * 8 * kHeadDim * 4 + kDecWarps * 16 * 4 <= kDecStages * kDecStageBytes,
-                "epilogue reuses the ring");
+  static_assert(epilogue_smem_bytes(kDecWarps) <= kDecStages * kDecStageBytes, "epilogue reuses the ring");
   auto kernel = nvfp4_decode_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
   if (e != cudaSuccess) return e;

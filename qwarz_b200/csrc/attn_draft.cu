@@ -245,14 +245,14 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
     }
   }
   __syncthreads();
-  decode_epilogue<kDrWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, true, [](int gg, int j) {
-    return j < 8 ? 16 * gg + 2 * j : 128 + 16 * gg + 2 * (j - 8);
+  decode_epilogue<kDrWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int d, int& gg, int& j) {
+    gg = (d & 127) >> 4;
+    j = ((d >> 7) << 3) + ((d & 15) >> 1);
   });
 }
 
 cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream) {
-  static_assert(kDrWarps * 8 * kHeadDim * 4 + kDrWarps * 16 * 4 <= kDrStages * kDrStageBytes,
-                "epilogue reuses the ring");
+  static_assert(epilogue_smem_bytes(kDrWarps) <= kDrStages * kDrStageBytes, "epilogue reuses the ring");
   cudaError_t e = cudaFuncSetAttribute(fp8_draft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kDrSmemBytes);
   if (e != cudaSuccess) return e;
