@@ -186,7 +186,6 @@ def cpu_layers_for_oracle(device_layers, queries, n: int):
 
 # -------------------------------------------------------------- our arm
 def run_ours(args, rank: int, world: int, device) -> dict | None:
-    from qwarz_b200 import attention as qattn
     from qwarz_b200 import build, ops, sharded
 
     build.build()
@@ -267,46 +266,36 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
     ms_step = t_ms / args.steps
     split_ms_launch = t_split_ms / args.steps / LAYERS
 
-    # ----- end to end through the public API, host copies inside the graph
-    h2d = LAYERS * (q[0].numel() + knew[0].numel() + vnew[0].numel()) * 2
-    d2h = LAYERS * out[0].numel() * 2
+    # ----- end to end through the public API, host copies inside the graph:
+    # one pinned H2D of the step's inputs (q, k, v of every layer, one
+    # buffer) and one D2H of the step's outputs, per-layer calls on views.
+    per_in = HEADS * DIM + 2 * KV_HEADS * DIM
+    host_in = torch.empty(LAYERS, per_in, dtype=dtype).pin_memory()
+    for l in range(LAYERS):
+        host_in[l].copy_(torch.cat([q[l].flatten(), knew[l].flatten(), vnew[l].flatten()]).cpu())
+    host_out = torch.empty(LAYERS, HEADS * DIM, dtype=dtype).pin_memory()
+    dev_in = torch.empty(LAYERS, per_in, dtype=dtype, device=device)
+    dev_out = torch.empty(LAYERS, HEADS * DIM, dtype=dtype, device=device)
+    dq = [dev_in[l, :HEADS * DIM].view(1, 1, HEADS, DIM) for l in range(LAYERS)]
+    dk = [dev_in[l, HEADS * DIM:HEADS * DIM + KV_HEADS * DIM].view(1, 1, KV_HEADS, DIM) for l in range(LAYERS)]
+    dv = [dev_in[l, HEADS * DIM + KV_HEADS * DIM:].view(1, 1, KV_HEADS, DIM) for l in range(LAYERS)]
+    do = [dev_out[l].view(1, 1, HEADS, DIM) for l in range(LAYERS)]
+    h2d = host_in.numel() * host_in.element_size()
+    d2h = host_out.numel() * host_out.element_size()
     if world == 1:
-        host_q = [t.cpu().pin_memory() for t in q]
-        host_k = [t.cpu().pin_memory() for t in knew]
-        host_v = [t.cpu().pin_memory() for t in vnew]
-        host_o = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in out]
-        dq = [torch.empty_like(t) for t in q]
-        dk = [torch.empty_like(t) for t in knew]
-        dv = [torch.empty_like(t) for t in vnew]
-
-        tables = [layers[l][1].view(1, -1) for l in range(LAYERS)]
-
         def e2e_step():
+            dev_in.copy_(host_in, non_blocking=True)
             for l in range(LAYERS):
-                dq[l].copy_(host_q[l], non_blocking=True)
-                dk[l].copy_(host_k[l], non_blocking=True)
-                dv[l].copy_(host_v[l], non_blocking=True)
-                res = qattn.attend(dq[l], dk[l], dv[l], layers[l][0], pre, block_table=tables[l])
-                host_o[l].copy_(res, non_blocking=True)
-
-        qattn.release_attention_plans()
-    else:
-        host_q = [t.cpu().pin_memory() for t in q]
-        host_k = [t.cpu().pin_memory() for t in knew]
-        host_v = [t.cpu().pin_memory() for t in vnew]
-        host_o = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in out]
-        dq = [torch.empty_like(t) for t in q]
-        dk = [torch.empty_like(t) for t in knew]
-        dv = [torch.empty_like(t) for t in vnew]
-
-        def e2e_step():
-            for l in range(LAYERS):
-                dq[l].copy_(host_q[l], non_blocking=True)
-                dk[l].copy_(host_k[l], non_blocking=True)
-                dv[l].copy_(host_v[l], non_blocking=True)
                 cache, perm = layers[l]
-                res = dec.step(dq[l], dk[l], dv[l], cache, perm, pre, out[l])
-                host_o[l].copy_(res, non_blocking=True)
+                ops.nvfp4_attend(dq[l], dk[l], dv[l], *cache, perm, pre, do[l], po, pml, splits)
+            host_out.copy_(dev_out, non_blocking=True)
+    else:
+        def e2e_step():
+            dev_in.copy_(host_in, non_blocking=True)
+            for l in range(LAYERS):
+                cache, perm = layers[l]
+                dec.step(dq[l], dk[l], dv[l], cache, perm, pre, do[l])
+            host_out.copy_(dev_out, non_blocking=True)
 
     e2e_graph = capture(e2e_step)
     for _ in range(args.warmup):
@@ -381,13 +370,15 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
             "us_per_step": e2e_ms * 1e3,
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
-            "api": ("qwarz_b200.attention.attend per layer" if world == 1 else
+            "api": ("qwz_nvfp4_attend (C ABI, via qwarz_b200.ops.nvfp4_attend) per layer" if world == 1 else
                     "qwarz_b200.sharded.ShardedDecode.step per layer (NCCL all-gather inside)")
-                   + ", pinned H2D/D2H, captured in one CUDA graph, max over ranks",
+                   + "; one pinned H2D of the step's q/k/v and one D2H of its outputs; "
+                     "captured in one CUDA graph, max over ranks",
         },
-        # our kernels per timed step: append, split, combine (+ shard combine at N>1),
-        # plus the split-only roofline graph
-        "gpu_launches": args.steps * LAYERS * (3 if world == 1 else 4) + args.steps * LAYERS,
+        # our kernels per timed step: split with fused append + combine (N=1);
+        # append, split, partial combine, gathered combine (N>1); plus the
+        # split-only roofline graph
+        "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 4) + args.steps * LAYERS,
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:

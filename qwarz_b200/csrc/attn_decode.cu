@@ -26,6 +26,7 @@
 // Waits are bounded (kErrTimeout instead of a hang).
 
 #include "attn_common.cuh"
+#include "nvfp4_quant.cuh"
 
 namespace qwz {
 
@@ -180,6 +181,23 @@ QWZ_DEVINL void issue_page(const SplitParams& p, const int* pid, DecMeta* meta, 
   tma_load_2d(dst + 2 * kDecCodeTile + kDecScaleTile, &p.tm_vs, kvh * kScaleBytes, y, fb);
 }
 
+// Fused append of the new row: warp kDecWarps-2 writes K, kDecWarps-1 V,
+// for this CTA's KV head, then fences so the page's TMA read sees the bytes
+// (the same page lookup and error reporting as nvfp4_append_kernel).
+template <typename T>
+QWZ_DEVINL void fused_append(const SplitParams& p, int pos, int kvh, int warp, int lane) {
+  const int tensor = warp - (kDecWarps - 2);
+  const int pp = lookup_page(p, pos, lane == 0 && tensor == 0);
+  if (pp < 0) return;
+  const size_t row = ((size_t)pp * kPage + (pos & (kPage - 1))) * kKvHeads + kvh;
+  const T* src = reinterpret_cast<const T*>(tensor ? p.app_v : p.app_k) + (size_t)kvh * kHeadDim;
+  uint8_t* codes = const_cast<uint8_t*>(tensor ? p.v_codes : p.k_codes) + row * kCodeBytes;
+  uint8_t* scales = const_cast<uint8_t*>(tensor ? p.v_scales : p.k_scales) + row * kScaleBytes;
+  quant::quantize_row_lane<T>(src, codes, scales, lane);
+  __threadfence();
+  fence_proxy_async_global();
+}
+
 }  // namespace
 
 template <typename T>
@@ -211,6 +229,15 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
     const int i = tid + r * kDecWarps * 32;
     if (i < n_cached) pid[i] = row[r];
   }
+  // fused append: the new row's page is this CTA's page k_app (its last)
+  int k_app = -1, app_pos = 0;
+  if (p.app_k != nullptr) {
+    app_pos = __ldg(p.seqlens);
+    const int st = (app_pos - p.tok_begin) >> 8;
+    if (app_pos >= p.tok_begin && st >= rg.st_lo && st < rg.st_lo + rg.n_st) k_app = st - rg.st_lo;
+  }
+  const bool app_warp = k_app >= 0 && warp >= kDecWarps - 2;
+  if (app_warp && k_app < kDecStages) fused_append<T>(p, app_pos, kvh, warp, lane);  // before the first issue
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kDecStages; ++s) {
@@ -229,6 +256,9 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
     for (int k = 0; k < min(rg.n_st, kDecStages); ++k)
       issue_page(p, pid, meta, rg, k, k, sbase, bar_full, kvh);
   }
+  // A later page is issued by the last releaser of an iteration these two
+  // warps reach only after writing (release: __threadfence_block + atomic).
+  if (app_warp && k_app >= kDecStages) fused_append<T>(p, app_pos, kvh, warp, lane);
 
   float o[16][4];
 #pragma unroll

@@ -298,10 +298,17 @@ int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache,
   rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
                   partial_o, partial_ml, table_width, num_pages, q_len, num_splits, 0, sm_scale);
   if (rc) return rc;
-  rc = qwz_nvfp4_append(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
-                        table_width, q_len, qwz::kKvHeads, qwz::kPage, qwz::kHeadDim, num_pages,
-                        dtype, stream);
-  if (rc) return rc;
+  if (q_len == 1) {  // the decode kernel writes the new row itself (one launch fewer)
+    if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
+      return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+    p.app_k = k;
+    p.app_v = v;
+  } else {
+    rc = qwz_nvfp4_append(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                          table_width, q_len, qwz::kKvHeads, qwz::kPage, qwz::kHeadDim, num_pages,
+                          dtype, stream);
+    if (rc) return rc;
+  }
   rc = launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_nvfp4_attend(split)");
   if (rc) return rc;
   const qwz::CombineParams c =

@@ -211,6 +211,11 @@ QWZ_DEVINL void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32
 QWZ_DEVINL void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) reads of the same bytes.
+QWZ_DEVINL void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
+}
 QWZ_DEVINL void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

@@ -39,6 +39,12 @@ struct alignas(64) SplitParams {
   int split_len;                 // >0: fixed tokens per split (multiple of 256); 0: balanced
   int num_splits;
   float sm_scale_log2;           // sm_scale * log2(e)
+  // Fused append (NVFP4 decode, q_len 1, through qwz_nvfp4_attend): the new
+  // K/V row [4, 256] (same type as q) for token seqlens[0]; the CTA owning
+  // that token's page quantises it into the pool before reading the page.
+  // Null: no append.
+  const void* app_k;
+  const void* app_v;
 };
 
 // LSE combine of split partials.  Row r, split s reads

@@ -227,6 +227,68 @@ def test_known_answer_uniform_softmax(cuda):
     np.testing.assert_array_equal(out[:, :, 2:].numpy(), 0.0)
 
 
+# ------------------------------------------------- attend (append + attention)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("pre,splits", [(0, 1), (255, 3), (256, 37), (1023, 1), (2900, 1), (2900, 5),
+                                        (2900, 37)])
+def test_attend_q1_writes_the_row_and_attends_over_it(cuda, dtype, pre, splits):
+    """q_len 1 through qwz_nvfp4_attend: the decode kernel writes the new row
+    itself.  The pool must hold the oracle writer's bytes and the output must
+    match the oracle over it, whether the row's page is one of the owning
+    CTA's first three pages (1023/1 is the fourth; 2900/1 the twelfth)."""
+    from qwarz_b200 import _lib, ops
+
+    pages = 12
+    table = rng.permutation(400 + pre, pages)
+    c, _, _ = make_cache(401, pre, pages, table)
+    kn = torch.from_numpy(cases.kv_rows(402 + pre, 1)).to(dtype)
+    vn = torch.from_numpy(cases.kv_rows(403 + pre, 1)).to(dtype)
+    ref = {n: c[n].copy() for n in ("k_cache", "v_cache", "k_scales", "v_scales", "table")}
+    nvfp4.append(kn.float().numpy(), vn.float().numpy(), ref["k_cache"], ref["v_cache"],
+                 ref["k_scales"], ref["v_scales"], table, pre)
+    dc = to_device(c, cuda)
+    q = queries(404 + pre, 1, dtype).to(cuda)
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    po, pml = ops.split_workspace(cuda, 1, splits)
+    out = torch.empty_like(q)
+    _lib.device_error(clear=True)
+    ops.nvfp4_attend(q, kn.to(cuda), vn.to(cuda), dc["k_cache"], dc["v_cache"], dc["k_scales"],
+                     dc["v_scales"], dc["table"], lens, out, po, pml, splits)
+    torch.cuda.synchronize()
+    for n in ("k_cache", "v_cache", "k_scales", "v_scales"):
+        np.testing.assert_array_equal(dc[n].view(torch.uint8).cpu().numpy(), ref[n], err_msg=n)
+    expect = oatt.nvfp4_attention(q.float().cpu(), **{k: v for k, v in to_cpu_torch(ref).items() if k != "table"},
+                                  block_table=torch.from_numpy(table), pre_len=pre)
+    assert_close_attention(out.float().cpu().numpy(), expect.numpy(),
+                           f"attend q1 pre={pre} splits={splits} {dtype}", str(dtype).split(".")[-1])
+    assert _lib.device_error(clear=True) == 0
+
+
+def test_attend_q1_row_beyond_the_table_is_reported(cuda):
+    """A full table: the new row has no page.  Nothing is written, the table
+    overrun is reported, and the output stays finite."""
+    from qwarz_b200 import _lib, ops
+
+    pages, pre = 2, 512
+    table = np.array([1, 0], np.int32)
+    c, _, _ = make_cache(410, pre, pages, table)
+    dc = to_device(c, cuda)
+    before = {n: dc[n].clone() for n in ("k_cache", "v_cache", "k_scales", "v_scales")}
+    q = queries(411, 1).to(cuda)
+    kn = torch.ones(1, 4, 256, dtype=torch.float16, device=cuda)
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    po, pml = ops.split_workspace(cuda, 1, 3)
+    out = torch.empty_like(q)
+    _lib.device_error(clear=True)
+    ops.nvfp4_attend(q, kn, kn, dc["k_cache"], dc["v_cache"], dc["k_scales"], dc["v_scales"],
+                     dc["table"], lens, out, po, pml, 3)
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) & 1  # QWZ_DEVERR_TABLE_RANGE
+    assert torch.isfinite(out.float()).all()
+    for n, t in before.items():
+        assert torch.equal(dc[n].view(torch.uint8), t.view(torch.uint8)), n
+
+
 # -------------------------------------------------------------------- draft
 def test_draft_vs_reference_golden(cuda, golden):
     from qwarz_b200.draft_attention import DecodeAttention
