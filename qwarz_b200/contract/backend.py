@@ -23,12 +23,15 @@ COMBINE_INT32_ARG_INDEX = (4,)
 # Launch policy of the sm_100a kernels (cf. the reference's
 # hybrid.DECODE_POLICY for its Triton Attention64 split kernel).
 DECODE_POLICY = {
-    "q1": {"kernel": "nvfp4_decode_kernel", "warps": 4, "stage_tokens": 64, "stages": 4,
-           "mma": "m16n8k16 tokens x heads(6->8)", "ctas_per_sm": 2},
-    "q2-8": {"kernel": "nvfp4_verify_kernel", "warps": 4, "stage_tokens": 64, "stages": 3,
-             "mma": "m16n8k16 tokens x rows(6*q_len->8*NT)", "ctas_per_sm": 2},
-    "draft": {"kernel": "fp8_decode_kernel", "warps": 4, "stage_tokens": 64, "stages": 3,
-              "splits": 16},
+    "q1": {"kernel": "nvfp4_decode_kernel", "warps": 8, "stage_tokens": 256, "stages": 3,
+           "copy": "TMA 2-D boxes, 128-byte swizzle", "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
+           "ctas_per_sm": 1, "append": "fused when called through qwz_nvfp4_attend"},
+    "q2-8": {"kernel": "nvfp4_verify_tc_kernel", "warps": 10, "roles": "TMA, MMA/TMEM owner, 8 math",
+             "stage_tokens": 128, "stages": 4, "copy": "TMA 2-D boxes, 128-byte swizzle",
+             "mma": "tcgen05 kind::f16 M=128: S^T = K Q^T (N=16/32/48), O^T = V^T [P_hi|P_lo]^T (N=2x)",
+             "tmem_columns": 512, "ctas_per_sm": 1},
+    "draft": {"kernel": "fp8_draft_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
+              "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37},
     "combine": {"kernel": "lse_combine_kernel", "threads": 256, "split_groups": 8},
 }
 

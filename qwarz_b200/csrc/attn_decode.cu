@@ -17,7 +17,7 @@
 // Warp w owns tokens 32w..32w+31 of every page as two independent 16-token
 // MMA tiles (A: +0..15, B: +16..31), which gives each warp two dependency
 // chains to interleave and one softmax update per 32 tokens.  Layout per
-// tile (see attn_split.cu for the derivation):
+// tile:
 //   QK  S^T[16 tok x 8 heads] = K[16 x 256] Q^T, tokens on M, the 6 GQA
 //       heads (padded to 8) on N, lane quad q's k-step s covering
 //       d = 64q + 4s + {0..3} so each A register is one code byte;

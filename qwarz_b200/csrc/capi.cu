@@ -91,17 +91,18 @@ int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t row
 }
 
 // Descriptors of the NVFP4 pool: codes [P*256, 512 B] (boxes of one head's
-// 128 B x one 256-token page, 128-byte swizzle), scales [P*256, 64 B]
-// (16 B x 256 boxes).
-int encode_pool(qwz::SplitParams& p, int32_t num_pages) {
+// 128 B x box_rows tokens, 128-byte swizzle), scales [P*256, 64 B] (16 B x
+// box_rows).  The decode kernel streams whole pages (256 rows), the verify
+// kernel 128-token tiles.
+int encode_pool(qwz::SplitParams& p, int32_t num_pages, uint32_t box_rows) {
   const uint64_t rows = (uint64_t)num_pages * qwz::kPage;
-  int rc = encode_2d(&p.tm_kc, p.k_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, qwz::kPage,
+  int rc = encode_2d(&p.tm_kc, p.k_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, box_rows,
                      CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_2d(&p.tm_vc, p.v_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, qwz::kPage,
+  if (!rc) rc = encode_2d(&p.tm_vc, p.v_codes, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, box_rows,
                           CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!rc) rc = encode_2d(&p.tm_ks, p.k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, qwz::kPage,
+  if (!rc) rc = encode_2d(&p.tm_ks, p.k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, box_rows,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (!rc) rc = encode_2d(&p.tm_vs, p.v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, qwz::kPage,
+  if (!rc) rc = encode_2d(&p.tm_vs, p.v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, box_rows,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
   return rc;
 }
@@ -143,7 +144,7 @@ int fill_split(qwz::SplitParams& p, const void* q, const void* kc, const void* v
   p.split_len = split_len;
   p.num_splits = num_splits;
   p.sm_scale_log2 = sm_scale * kLog2e;
-  return encode_pool(p, num_pages);
+  return encode_pool(p, num_pages, q_len == 1 ? qwz::kPage : 128u);
 }
 
 qwz::CombineParams split_combine_params(const float* po, const float* pml, int rows, int splits,

@@ -93,15 +93,10 @@ def sm_count(device) -> int:
 
 
 def default_splits(device, max_tokens: int, q_len: int = 1) -> int:
-    """Splits per KV head.  Decode (q_len 1): one CTA per SM, at least one
-    256-token page per split.  Verify: two CTAs per SM, at least two 64-token
-    stages per split."""
-    if q_len == 1:
-        pages = max(1, math.ceil(max_tokens / PAGE))
-        return int(max(1, min(sm_count(device) // KV_HEADS, pages)))
-    stages = max(1, math.ceil(max_tokens / 64))
-    target = max(1, (2 * sm_count(device)) // KV_HEADS)
-    return int(max(1, min(target, stages // 2 if stages >= 2 else 1)))
+    """Splits per KV head: one CTA per SM (decode and verify kernels both
+    hold a whole SM), at least one 256-token page per split."""
+    pages = max(1, math.ceil(max_tokens / PAGE))
+    return int(max(1, min(sm_count(device) // KV_HEADS, pages)))
 
 
 def split_workspace(device, q_len: int, num_splits: int):
