@@ -1,36 +1,39 @@
 // NVFP4 paged MTP verify (q_len 2..8) on the fifth-generation tensor cores
-// (tcgen05: operands and accumulators in tensor memory), sm_100a.
+// (tcgen05: accumulators in tensor memory), sm_100a.
 //
 // Replaces the q_len > 1 XQA launch of src/qwasar_runtime/xqa.py:484-554
 // (MTP verify: q_len query rows per head, lower-right causal, xqa.py:662)
 // behind the split ABI of tests/test_attention_kernel_abi.py:13-32.
 //
-// CTA = one KV head x one split (a run of pages), 10 warps:
-//   warp 0     TMA producer: 128-token stages (codes + scales of K and V,
-//              36 KB) into a 4-deep ring (full / empty mbarriers);
-//   warp 1     TMEM owner (512 columns) and MMA issuer (one thread);
-//   warps 2-9  eight math warps: warp w serves TMEM lane quadrant q = w % 4
-//              and half h = (w - 2) / 4 of the work.
-// Per 128-token tile:
-//   1. math: K (E2M1 x E4M3 -> FP16, exact) into TMEM as the A operand,
-//      lane = token, column = head-dim pair (32x32b stores, thread = token);
-//   2. MMA:  S^T[128 tok x N] = K Q^T, N = 6 q_len rounded up to 16, Q in
-//      shared memory (K-major, 128-byte swizzle, rows scaled by a power of
-//      two so BF16 queries convert to FP16 exactly);
-//   3. math: V^T into TMEM, lane = head-dim (two M=128 halves), column =
-//      token pair, built in mma-fragment registers and written with 16x256b
-//      stores; tokens inside each 16-token step are permuted (kperm) and the
-//      head-dim order on the lanes is d = 32g + 2x + e (see vt_lane_d);
-//   4. math: base-2 online softmax on S^T (thread = token): the reference
-//      max of a column only moves when a score exceeds it by kLazy (then O
-//      is rescaled in TMEM); P = hi + lo in FP16 is written to shared
-//      memory as the K-major operand [2N rows (hi | lo) x 128 tokens];
-//   5. MMA:  O^T[256 d x 2N] += V^T [P_hi | P_lo]^T (one MMA per M half and
-//      16-token step reads V^T once for both halves of P).
-// The epilogue adds the hi and lo halves of O^T and writes one (m, l, O)
-// record per query row and split, the layout lse_combine_kernel reads.
-// Every wait is bounded; the math warps decide timeouts collectively at a
-// per-tile vote, so named barriers never wait for a warp that left.
+// CTA = one KV head x one split (a run of pages), 11 warps:
+//   warp 0      TMA producer of K tiles (codes + scales, 18 KB per 128
+//               tokens) into a 3-deep ring;
+//   warp 1      TMEM owner (512 columns) and MMA issuer (one thread);
+//   warp 2      TMA producer of V tiles into a 2-deep ring;
+//   warps 3-10  eight math warps: warp w serves TMEM lane quadrant q = w % 4
+//               and half h = (w - 3) / 4 of the work.
+// Per 128-token tile i (tokens on the MMA M dimension, head-dim d):
+//   K(i)    math: E2M1 x E4M3 -> FP16 (exact) into TMEM as the A operand,
+//           lane = token, column = d pair (32x32b stores, thread = token);
+//   QK(i)   MMA:  S^T[128 tok x N] = K Q^T into one of two S buffers, N =
+//           6 q_len rounded up to 16, Q in shared memory (K-major, 128-byte
+//           swizzle, rows scaled by a power of two so BF16 queries convert
+//           to FP16 exactly);
+//   soft(i) math: base-2 online softmax on S^T (thread = token): the
+//           reference max of a column only moves when a score exceeds it by
+//           kLazy (then O is rescaled in TMEM); P = hi + lo in FP16;
+//   V(i)    math: V -> FP16 rows [token][d] in shared memory (the MN-major A
+//           operand of PV), P -> [token][hi | lo] (the MN-major B operand);
+//   PV(i)   MMA:  O^T[256 d x 2N] += V^T [P_hi | P_lo]^T, two M=128 halves
+//           of d, V^T read once for both halves of P.
+// Order: the math warps dequantise K(i+1) as soon as S(i) is read, so
+// QK(i+1) is queued ahead of PV(i); they write V(i) and P(i) only after
+// PV(i-1) has finished with the single V and P buffers, which by then it
+// long has.  The epilogue adds the hi and lo halves of O^T and writes one
+// (m, l, O) record per query row and split, the layout lse_combine_kernel
+// reads.  Every wait is bounded; the math warps decide timeouts
+// collectively at a per-tile vote, so named barriers never wait for a warp
+// that left.
 
 #include "attn_common.cuh"
 #include "tc_common.cuh"
@@ -39,43 +42,43 @@ namespace qwz {
 
 using namespace detail;
 
-constexpr int kVtWarps = 10;
-constexpr int kVtStages = 4;
+constexpr int kVtWarps = 11;
+constexpr int kVtMath0 = 3;                                // first math warp
+constexpr int kVtKStages = 3, kVtVStages = 2;
 constexpr int kVtTile = 128;
-constexpr int kVtCodeBox = kVtTile * kCodeBytes;                         // 16 KB
-constexpr int kVtScaleBox = kVtTile * kScaleBytes;                       // 2 KB
-constexpr int kVtStageBytes = 2 * kVtCodeBox + 2 * kVtScaleBox;          // 36 KB
+constexpr int kVtCodeBox = kVtTile * kCodeBytes;           // 16 KB
+constexpr int kVtScaleBox = kVtTile * kScaleBytes;         // 2 KB
+constexpr int kVtHalfStage = kVtCodeBox + kVtScaleBox;     // 18 KB (K or V of one tile)
 constexpr int kVtPidCache = 512;
-// TMEM columns: K (A of QK) | V^T halves (A of PV) | S^T | O^T halves
-constexpr uint32_t kTmK = 0, kTmV = 128, kTmS = 256, kTmO = 320;
+// TMEM columns: K (A of QK) | S^T buffer 0 | S^T buffer 1 | O^T halves
+constexpr uint32_t kTmK = 0, kTmS = 128, kTmO = 256;
 constexpr uint32_t kTmCols = 512;
 
 template <int N>
 struct VtLayout {
-  static constexpr int kQ = kVtStages * kVtStageBytes;      // Q operand: 4 k-atoms [N x 128 B]
-  static constexpr int kP = kQ + N * 512;                   // P operand: 2 k-atoms [2N x 128 B]
-  static constexpr int kBars = kP + 2 * N * 256;            // full[4] empty[4] k pv s o
-  static constexpr int kMeta = kBars + 8 * (2 * kVtStages + 4);  // stage_end[4], tmem, abort
-  static constexpr int kRowfac = kMeta + 32;                // [N]
-  static constexpr int kAlpha = kRowfac + 4 * N;            // [N]
-  static constexpr int kMref = kAlpha + 4 * N;              // [N]
-  static constexpr int kWred = kMref + 4 * N;               // [2 h][4 q][N / 2]
-  static constexpr int kPid = kWred + 4 * 4 * N;            // [kVtPidCache]
+  static constexpr int kKRing = 0;                                   // 3 x 18 KB
+  static constexpr int kVRing = kKRing + kVtKStages * kVtHalfStage;  // 2 x 18 KB
+  static constexpr int kVf = 92160;                                  // V FP16: [2h+a][128 tok][128 B]
+  static constexpr int kQ = kVf + 4 * 16384;                         // Q: 4 k-atoms [N x 128 B]
+  static constexpr int kPAtoms = (2 * N + 63) / 64;                  // P: n-atoms [128 tok][128 B]
+  static constexpr int kP = kQ + N * 512;
+  static constexpr int kBars = kP + kPAtoms * 16384;
+  // kfull[3] kempty[3] vfull[2] vempty[2] kready pvready s[2] o (15 x 8 B)
+  static constexpr int kMeta = kBars + 128;
+  static constexpr int kRowfac = kMeta + 32;                         // stage ends, tmem, abort, fin
+  static constexpr int kAlpha = kRowfac + 4 * N;
+  static constexpr int kMref = kAlpha + 4 * N;
+  static constexpr int kWred = kMref + 4 * N;                        // [2 h][4 q][N / 2]
+  static constexpr int kPid = kWred + 4 * 4 * N;
   static constexpr int kBytes = kPid + 4 * kVtPidCache + 1024;
+  static_assert(kVRing + kVtVStages * kVtHalfStage <= kVf && kVf % 1024 == 0, "ring / V layout");
+  static_assert(kQ % 1024 == 0 && kP % 1024 == 0 && kBars % 1024 == 0, "operand atoms are 1024-byte aligned");
+  static_assert(8 * (2 * kVtKStages + 2 * kVtVStages + 5) <= 128 && (kMeta + 24) % 8 == 0,
+                "mbarriers are 8-byte aligned");
+  static_assert(kRowfac % 16 == 0, "row factors are read as float4");
 };
 
 namespace {
-
-// Position of token t (0..15) of a 16-token step inside the PV K order that
-// the 16x256b V^T stores produce: column 2c holds tokens (2c, 2c+1) of the
-// step, column 2c+1 tokens (2c+8, 2c+9) (c = lane % 4).
-QWZ_DEVINL int kperm(int t) { return 4 * ((t & 7) >> 1) + 2 * (t >> 3) + (t & 1); }
-
-// Head-dim index held by V^T / O^T lane L of M half h.
-QWZ_DEVINL int vt_lane_d(int L, int h) {
-  const int x = 8 * h + (L >> 4), g = L & 7, e = (L >> 3) & 1;
-  return 32 * g + 2 * x + e;
-}
 
 QWZ_DEVINL void math_bar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
 QWZ_DEVINL bool math_bar_or(bool v) {
@@ -93,9 +96,6 @@ QWZ_DEVINL uint2 lds64(uint32_t addr) {
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(addr));
   return v;
 }
-QWZ_DEVINL void sts16(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.u16 [%0], %1;\n" ::"r"(addr), "h"((unsigned short)v));
-}
 QWZ_DEVINL void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d));
 }
@@ -110,7 +110,7 @@ QWZ_DEVINL float warp_sum(float v) {
   return v;
 }
 
-// TMEM loads of n (multiple of 8) consecutive columns into v.
+// TMEM loads of NC (multiple of 8) consecutive columns into v.
 template <int NC>
 QWZ_DEVINL void ld_cols(uint32_t taddr, float (&v)[NC]) {
   static_assert(NC % 8 == 0, "8-column granularity");
@@ -161,6 +161,36 @@ QWZ_DEVINL void stage_q(const SplitParams& p, int kvh, uint32_t qbase, float* ro
   }
 }
 
+// Head-dim half h of token row tt of a K or V tile (the 64 code bytes of
+// chunks 4h..4h+3, 128-byte swizzle, and their 8 scales) as f16x2 words in
+// d order, handed to put(c, r16) per 32 values (code chunk c).  `zero`
+// (rows at or past the valid end) makes every value 0.
+template <class Put>
+QWZ_DEVINL void dequant_row_half(uint32_t codes, uint32_t scales, int tt, int h, bool zero, Put put) {
+  uint2 sc = lds64(scales + tt * kScaleBytes + 8 * h);
+  if (zero) sc = make_uint2(0u, 0u);
+  uint32_t s01, s23, s45, s67;
+  e4m3x4_to_f16x2x2(sc.x, s01, s23);
+  e4m3x4_to_f16x2x2(sc.y, s45, s67);
+  const uint32_t spair[4] = {s01, s23, s45, s67};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 w = lds128(codes + tt * kCodeBytes + (((4 * h + c) ^ (tt & 7)) << 4));
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t sA = __byte_perm(spair[c], 0, 0x1010), sB = __byte_perm(spair[c], 0, 0x3232);
+    uint32_t r[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t hv[4];
+      e2m1x8_to_f16x2x4(wv[j], hv);
+      const uint32_t sc2 = j < 2 ? sA : sB;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) r[4 * j + e] = hmul2_u32(hv[e], sc2);
+    }
+    put(c, r);
+  }
+}
+
 }  // namespace
 
 template <typename T, int N>
@@ -174,11 +204,14 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   uint8_t* sg = smem + (sb - sraw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y;
-  const uint32_t bar_full = sb + L::kBars, bar_empty = bar_full + 8 * kVtStages;
-  const uint32_t bar_k = bar_empty + 8 * kVtStages, bar_pv = bar_k + 8, bar_s = bar_pv + 8, bar_o = bar_s + 8;
-  int* stage_end = reinterpret_cast<int*>(sg + L::kMeta);
+  const uint32_t bar_kfull = sb + L::kBars, bar_kempty = bar_kfull + 8 * kVtKStages;
+  const uint32_t bar_vfull = bar_kempty + 8 * kVtKStages, bar_vempty = bar_vfull + 8 * kVtVStages;
+  const uint32_t bar_kready = bar_vempty + 8 * kVtVStages, bar_pv = bar_kready + 8;
+  const uint32_t bar_s = bar_pv + 8, bar_o = bar_s + 16;  // bar_s: one per S buffer
+  int* kstage_end = reinterpret_cast<int*>(sg + L::kMeta);  // [kVtKStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sg + L::kMeta + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sg + L::kMeta + 20);
+  const uint32_t bar_fin = sb + L::kMeta + 24;  // the MMA thread's last commit
   float* rowfac = reinterpret_cast<float*>(sg + L::kRowfac);
   float* alpha_s = reinterpret_cast<float*>(sg + L::kAlpha);
   float* mref_s = reinterpret_cast<float*>(sg + L::kMref);
@@ -191,14 +224,21 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
 
   if (tid == 0) {
 #pragma unroll
-    for (int s = 0; s < kVtStages; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 8);
+    for (int s = 0; s < kVtKStages; ++s) {
+      mbar_init(bar_kfull + 8 * s, 1);
+      mbar_init(bar_kempty + 8 * s, 8);
     }
-    mbar_init(bar_k, 8);
+#pragma unroll
+    for (int s = 0; s < kVtVStages; ++s) {
+      mbar_init(bar_vfull + 8 * s, 1);
+      mbar_init(bar_vempty + 8 * s, 8);
+    }
+    mbar_init(bar_kready, 8);
     mbar_init(bar_pv, 8);
     mbar_init(bar_s, 1);
+    mbar_init(bar_s + 8, 1);
     mbar_init(bar_o, 1);
+    mbar_init(bar_fin, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -210,8 +250,8 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     for (int i = lane; i < min(rg.n_st, kVtPidCache); i += 32)
       pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
   }
-  if (warp >= 2) {
-    stage_q<T, N>(p, kvh, sb + L::kQ, rowfac, warp - 2, lane);
+  if (warp >= kVtMath0) {
+    stage_q<T, N>(p, kvh, sb + L::kQ, rowfac, warp - kVtMath0, lane);
     fence_proxy_async_smem();  // Q is read by the tensor core
   }
   tc::fence_before();
@@ -219,87 +259,91 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   tc::fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 2) {
+    // ----------------------------------------------- producers (K: 0, V: 2)
+    const bool is_k = warp == 0;
+    const int nst = is_k ? kVtKStages : kVtVStages;
+    const uint32_t ring = sb + (is_k ? L::kKRing : L::kVRing);
+    const uint32_t full = is_k ? bar_kfull : bar_vfull, empty = is_k ? bar_kempty : bar_vempty;
+    const CUtensorMap* tm_c = is_k ? &p.tm_kc : &p.tm_vc;
+    const CUtensorMap* tm_s = is_k ? &p.tm_ks : &p.tm_vs;
     if (lane == 0 && n_tiles > 0) {
-      tma_prefetch_desc(&p.tm_kc);
-      tma_prefetch_desc(&p.tm_vc);
-      tma_prefetch_desc(&p.tm_ks);
-      tma_prefetch_desc(&p.tm_vs);
+      tma_prefetch_desc(tm_c);
+      tma_prefetch_desc(tm_s);
       int issued = 0;
       for (int i = 0; i < n_tiles; ++i) {
-        const int s = i % kVtStages;
+        const int s = i % nst;
         if (*abort_flag) break;
-        if (i >= kVtStages && !mbar_wait(bar_empty + 8 * s, ((i / kVtStages) - 1) & 1)) {
+        if (i >= nst && !mbar_wait(empty + 8 * s, ((i / nst) - 1) & 1)) {
           flag_error(kErrTimeout);
           *abort_flag = 1;
           break;
         }
         const int k = i >> 1;
         const int t0 = p.tok_begin + (rg.st_lo + k) * kPage + kVtTile * (i & 1);
-        const int pp = k < kVtPidCache ? pid[k] : lookup_page(p, t0, true);
-        stage_end[s] = pp >= 0 ? rg.tok_end : t0;  // released by the arrive below
-        const uint32_t fb = bar_full + 8 * s;
+        const int pp = k < kVtPidCache ? pid[k] : lookup_page(p, t0, is_k);
+        if (is_k) kstage_end[s] = pp >= 0 ? rg.tok_end : t0;  // released by the arrive below
+        const uint32_t fb = full + 8 * s;
         issued = i + 1;
         if (pp < 0) {  // bad page id: no copy; the math warps mask the tile
           mbar_arrive(fb);
           continue;
         }
-        mbar_arrive_expect_tx(fb, kVtStageBytes);
-        const uint32_t dst = sb + s * kVtStageBytes;
+        mbar_arrive_expect_tx(fb, kVtHalfStage);
+        const uint32_t dst = ring + s * kVtHalfStage;
         const int y = pp * kPage + kVtTile * (i & 1);
-        tma_load_2d(dst, &p.tm_kc, kvh * kCodeBytes, y, fb);
-        tma_load_2d(dst + kVtCodeBox, &p.tm_vc, kvh * kCodeBytes, y, fb);
-        tma_load_2d(dst + 2 * kVtCodeBox, &p.tm_ks, kvh * kScaleBytes, y, fb);
-        tma_load_2d(dst + 2 * kVtCodeBox + kVtScaleBox, &p.tm_vs, kvh * kScaleBytes, y, fb);
+        tma_load_2d(dst, tm_c, kvh * kCodeBytes, y, fb);
+        tma_load_2d(dst + kVtCodeBox, tm_s, kvh * kScaleBytes, y, fb);
       }
       // never leave with copies in flight (only reachable after an abort)
-      for (int i = max(issued - kVtStages, 0); i < issued; ++i)
-        if (!mbar_wait(bar_full + 8 * (i % kVtStages), (i / kVtStages) & 1)) flag_error(kErrTimeout);
+      for (int i = max(issued - nst, 0); i < issued; ++i)
+        if (!mbar_wait(full + 8 * (i % nst), (i / nst) & 1)) flag_error(kErrTimeout);
     }
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_qk = tc::idesc_f16_f32(128, N);
-      constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, 2 * N);
-      int committed = 0;
-      for (int i = 0; i < n_tiles; ++i) {
-        if (*abort_flag) break;
-        if (!mbar_wait(bar_k, i & 1)) {
-          flag_error(kErrTimeout);
-          *abort_flag = 1;
-          break;
-        }
+      constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, 2 * N, true, true);
+      auto qk = [&](int j) -> bool {
+        if (!mbar_wait(bar_kready, j & 1)) return false;
         tc::fence_after();
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks)
-          tc::mma_ts(tbase + kTmS, tbase + kTmK + 8 * ks,
+          tc::mma_ts(tbase + kTmS + 64 * (j & 1), tbase + kTmK + 8 * ks,
                      tc::smem_desc_k128(sb + L::kQ + (ks >> 2) * (N * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
-        tc::commit(bar_s);
-        if (!mbar_wait(bar_pv, i & 1)) {
-          flag_error(kErrTimeout);
-          *abort_flag = 1;
-          break;
-        }
+        tc::commit(bar_s + 8 * (j & 1));
+        return true;
+      };
+      bool fine = qk(0);
+      for (int i = 0; fine && i < n_tiles; ++i) {
+        if (*abort_flag) break;
+        if (i + 1 < n_tiles && !(fine = qk(i + 1))) break;
+        if (!(fine = mbar_wait(bar_pv, i & 1))) break;
         tc::fence_after();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            tc::mma_ts(tbase + kTmO + 2 * N * h, tbase + kTmV + 64 * h + 8 * ks,
-                       tc::smem_desc_k128(sb + L::kP + (ks >> 2) * (2 * N * 128) + (ks & 3) * 32), idesc_pv,
-                       (i > 0 || ks > 0));
+            tc::mma_ss(tbase + kTmO + 2 * N * h,
+                       tc::smem_desc_mn128(sb + L::kVf + 2 * h * 16384 + ks * 2048, 16384, 1024),
+                       tc::smem_desc_mn128(sb + L::kP + ks * 2048, 16384, 1024), idesc_pv, (i > 0 || ks > 0));
         }
         tc::commit(bar_o);
-        committed = i + 1;
       }
-      if (*abort_flag && committed > 0 && !mbar_wait(bar_o, (committed - 1) & 1)) flag_error(kErrTimeout);
+      if (!fine) {
+        flag_error(kErrTimeout);
+        *abort_flag = 1;
+      }
+      // never leave with MMAs in flight: one more commit covers every
+      // tcgen05.mma issued so far
+      tc::commit(bar_fin);
+      if (!mbar_wait(bar_fin, 0)) flag_error(kErrTimeout);
     }
   } else {
     // ---------------------------------------------------------------- math
-    const int q = warp & 3, h = (warp - 2) >> 2;
-    const int g = lane >> 2, qd = lane & 3;
+    const int q = warp & 3, h = (warp - kVtMath0) >> 2;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    const int tt = 32 * q + lane;  // this thread's token row of K, V, S^T and P
     float lsum[NH], mreg[NH];
 #pragma unroll
     for (int c = 0; c < NH; ++c) {
@@ -307,108 +351,66 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       mreg[c] = -CUDART_INF_F;
     }
     bool ok = true;
-    int done_tiles = 0;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int s = i % kVtStages;
-      const uint32_t st = sb + s * kVtStageBytes;
-      ok &= mbar_wait(bar_full + 8 * s, (i / kVtStages) & 1);
-      const int t0 = p.tok_begin + (rg.st_lo + (i >> 1)) * kPage + kVtTile * (i & 1);
-      const int vend = stage_end[s];
 
-      // (1) K -> TMEM, thread = token tt, head-dim half h
-      {
-        const int tt = 32 * q + lane;
-        const uint2 sc = lds64(st + 2 * kVtCodeBox + tt * kScaleBytes + 8 * h);
-        uint32_t s01, s23, s45, s67;
-        e4m3x4_to_f16x2x2(sc.x, s01, s23);
-        e4m3x4_to_f16x2x2(sc.y, s45, s67);
-        const uint32_t spair[4] = {s01, s23, s45, s67};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 w = lds128(st + tt * kCodeBytes + (((4 * h + c) ^ (tt & 7)) << 4));
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-          const uint32_t sA = __byte_perm(spair[c], 0, 0x1010), sB = __byte_perm(spair[c], 0, 0x3232);
-          uint32_t r[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint32_t hv[4];
-            e2m1x8_to_f16x2x4(wv[j], hv);
-            const uint32_t sc2 = j < 2 ? sA : sB;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) r[4 * j + e] = hmul2_u32(hv[e], sc2);
-          }
-          tc::st_32x32b_x16(tbase + lane_base + kTmK + 64 * h + 16 * c, r);
-        }
-      }
+    // K(j) -> TMEM, thread = token tt, head-dim half h (columns 64h ..);
+    // returns the tile's valid end, read before the ring slot is released
+    auto do_k = [&](int j) -> int {
+      const int s = j % kVtKStages;
+      ok &= mbar_wait(bar_kfull + 8 * s, (j / kVtKStages) & 1);
+      const int end = kstage_end[s];
+      const uint32_t st = sb + L::kKRing + s * kVtHalfStage;
+      const uint32_t col = tbase + lane_base + kTmK + 64 * h;
+      dequant_row_half(st, st + kVtCodeBox, tt, h, false,
+                       [&](int c, const uint32_t (&r)[16]) { tc::st_32x32b_x16(col + 16 * c, r); });
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_kempty + 8 * s);
       tc::wait_st();
       tc::fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_k);
+      if (lane == 0) mbar_arrive(bar_kready);
+      return end;
+    };
 
-      // (3) V^T -> TMEM after PV of the previous tile
-      if (i > 0) ok &= mbar_wait(bar_o, (i - 1) & 1);
+    int vend_next = n_tiles > 0 ? do_k(0) : 0;
+    int done_tiles = 0;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int sbuf = i & 1;
+      ok &= mbar_wait(bar_s + 8 * sbuf, (i >> 1) & 1);
       tc::fence_after();
-      {
-        const uint32_t vcode = st + kVtCodeBox, vscale = st + 2 * kVtCodeBox + kVtScaleBox;
-        const int lo = 8 * h + 2 * q;                // byte of m-tile x0 = 8h + 2q within chunk g
-        const bool tail = t0 + kVtTile > vend;
-#pragma unroll 2
-        for (int b = 0; b < 8; ++b) {
-          const int ta = 16 * b + 2 * qd;
-          const uint32_t va = lds16(vcode + ta * kCodeBytes + ((g ^ (ta & 7)) << 4) + lo);
-          const uint32_t vb = lds16(vcode + (ta + 1) * kCodeBytes + ((g ^ ((ta + 1) & 7)) << 4) + lo);
-          const uint32_t vc = lds16(vcode + (ta + 8) * kCodeBytes + ((g ^ ((ta + 8) & 7)) << 4) + lo);
-          const uint32_t vd = lds16(vcode + (ta + 9) * kCodeBytes + ((g ^ ((ta + 9) & 7)) << 4) + lo);
-          uint32_t sa = lds8(vscale + ta * kScaleBytes + 2 * g + h);
-          uint32_t sbb = lds8(vscale + (ta + 1) * kScaleBytes + 2 * g + h);
-          uint32_t sc = lds8(vscale + (ta + 8) * kScaleBytes + 2 * g + h);
-          uint32_t sd = lds8(vscale + (ta + 9) * kScaleBytes + 2 * g + h);
-          if (tail) {  // stale rows past the end add 0
-            if (t0 + ta >= vend) sa = 0;
-            if (t0 + ta + 1 >= vend) sbb = 0;
-            if (t0 + ta + 8 >= vend) sc = 0;
-            if (t0 + ta + 9 >= vend) sd = 0;
-          }
-          uint32_t sab, scd;
-          e4m3x4_to_f16x2x2(sa | (sbb << 8) | (sc << 16) | (sd << 24), sab, scd);
-          // byte j of X / Y: tokens (ta, ta+1) then (ta+8, ta+9), m-tiles x0, x0+1
-          const uint32_t xab = (va & 0x0F0Fu) | ((vb & 0x0F0Fu) << 4);
-          const uint32_t yab = ((va >> 4) & 0x0F0Fu) | (vb & 0xF0F0u);
-          const uint32_t xcd = (vc & 0x0F0Fu) | ((vd & 0x0F0Fu) << 4);
-          const uint32_t ycd = ((vc >> 4) & 0x0F0Fu) | (vd & 0xF0F0u);
-          uint32_t hx[4], hy[4];
-          e2m1x8_to_f16x2x4(xab | (xcd << 16), hx);
-          e2m1x8_to_f16x2x4(yab | (ycd << 16), hy);
-          const uint32_t col = tbase + kTmV + 64 * h + 8 * b;
-          tc::st_16x256b(col + lane_base, hmul2_u32(hx[0], sab), hmul2_u32(hx[2], scd), hmul2_u32(hy[0], sab),
-                         hmul2_u32(hy[2], scd));
-          tc::st_16x256b(col + lane_base + (16u << 16), hmul2_u32(hx[1], sab), hmul2_u32(hx[3], scd),
-                         hmul2_u32(hy[1], sab), hmul2_u32(hy[3], scd));
+      const int t0 = p.tok_begin + (rg.st_lo + (i >> 1)) * kPage + kVtTile * (i & 1);
+      const int vend = vend_next;
+
+      float x[NH];
+      ld_cols<NH>(tbase + lane_base + kTmS + 64 * sbuf + NH * h, x);
+      tc::wait_ld();
+      // S(i) is read and QK(i) is done: the K buffer takes K(i+1) now
+      if (i + 1 < n_tiles) vend_next = do_k(i + 1);
+
+      // ------------------------------------------------------- softmax(i)
+#pragma unroll
+      for (int c = 0; c < NH; c += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(rowfac + NH * h + c);
+        x[c] *= f.x;
+        x[c + 1] *= f.y;
+        x[c + 2] *= f.z;
+        x[c + 3] *= f.w;
+      }
+      // causal / length mask only on tiles that reach the end
+      if (t0 + kVtTile > min(vend, len_all - (p.q_len - 1))) {
+        const int tok = t0 + tt;
+#pragma unroll
+        for (int c = 0; c < NH; ++c) {
+          const int qi = min((NH * h + c) / kGroup, p.q_len - 1);
+          if (tok >= min(vend, len_all - (p.q_len - 1 - qi))) x[c] = -CUDART_INF_F;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_empty + 8 * s);  // stage read completely
-
-      // (4) softmax on S^T
-      ok &= mbar_wait(bar_s, i & 1);
-      tc::fence_after();
-      float x[NH];
-      ld_cols<NH>(tbase + lane_base + kTmS + NH * h, x);
-      tc::wait_ld();
-      const int tok = t0 + 32 * q + lane;
       bool need = false;
 #pragma unroll
-      for (int c = 0; c < NH; ++c) {
-        const int r = NH * h + c;
-        const int qi = min(r / kGroup, p.q_len - 1);
-        const int limit = min(vend, len_all - (p.q_len - 1 - qi));
-        x[c] = tok < limit ? x[c] * rowfac[r] : -CUDART_INF_F;
-        need |= x[c] > mreg[c] + kLazy;
-      }
+      for (int c = 0; c < NH; ++c) need |= x[c] > mreg[c] + kLazy;
       const bool bad = !ok || *abort_flag;
       if (math_bar_or(need || bad)) {
         if (math_bar_or(bad)) {
-          if (tid == 64) *abort_flag = 1;
+          if (tid == kVtMath0 * 32) *abort_flag = 1;
           flag_error(kErrTimeout);
           break;
         }
@@ -431,7 +433,9 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
           if (q == 0 && lane == 0) alpha_s[NH * h + c] = alpha;
         }
         math_bar();
-        if (i > 0) {  // O^T of this quadrant and half, both P halves
+        if (i > 0) {  // O^T of this quadrant and half, both P halves, after PV(i-1)
+          ok &= mbar_wait(bar_o, (i - 1) & 1);
+          tc::fence_after();
 #pragma unroll
           for (int c0 = 0; c0 < 2 * N; c0 += 16) {
             uint32_t r[16];
@@ -445,26 +449,49 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
         }
         math_bar();  // alpha_s / wred are rewritten by the next slow tile
       }
-      // P = hi + lo into the K-major operand, token tt at position kperm
-      {
-        const int tt = 32 * q + lane;
-        const int k = 16 * (tt >> 4) + kperm(tt & 15);
-        const uint32_t pk = sb + L::kP + (k >> 6) * (2 * N * 128) + ((k & 63) * 2 & 15);
-        const int chunk = ((k & 63) * 2) >> 4;
+      uint32_t hw[NH / 2], lw[NH / 2];
 #pragma unroll
-        for (int c = 0; c < NH; ++c) {
-          const float mu = mreg[c] == -CUDART_INF_F ? 0.f : mreg[c];
-          const float pv = exp2_approx(x[c] - mu);
-          lsum[c] += pv;
-          const __half hi = __float2half_rn(pv);
-          const __half lo = __float2half_rn(pv - __half2float(hi));
-          const int r = NH * h + c, r2 = N + r;
-          sts16(pk + r * 128 + ((chunk ^ (r & 7)) << 4), __half_as_ushort(hi));
-          sts16(pk + r2 * 128 + ((chunk ^ (r2 & 7)) << 4), __half_as_ushort(lo));
+      for (int j = 0; j < NH / 2; ++j) {
+        const float m0 = mreg[2 * j] == -CUDART_INF_F ? 0.f : mreg[2 * j];
+        const float m1 = mreg[2 * j + 1] == -CUDART_INF_F ? 0.f : mreg[2 * j + 1];
+        const float p0 = exp2_approx(x[2 * j] - m0), p1 = exp2_approx(x[2 * j + 1] - m1);
+        lsum[2 * j] += p0;
+        lsum[2 * j + 1] += p1;
+        hw[j] = pack_half2(p0, p1);
+        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
+        lw[j] = pack_half2(p0 - hf.x, p1 - hf.y);
+      }
+
+      // ------------------------------ V(i) and P(i) after PV(i-1) is done
+      if (i > 0) ok &= mbar_wait(bar_o, (i - 1) & 1);
+      {
+        const int s = i % kVtVStages;
+        ok &= mbar_wait(bar_vfull + 8 * s, (i / kVtVStages) & 1);
+        const uint32_t st = sb + L::kVRing + s * kVtHalfStage;
+        const uint32_t vrow = sb + L::kVf + 2 * h * 16384 + tt * 128;
+        dequant_row_half(st, st + kVtCodeBox, tt, h, t0 + tt >= vend, [&](int c, const uint32_t (&r)[16]) {
+          // d = 128h + 32c + 8j .. +7: atom 2h + c/2, 16-byte chunk 4(c%2) + j
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            sts128(vrow + (c >> 1) * 16384 + (((4 * (c & 1) + j) ^ (tt & 7)) << 4), r[4 * j], r[4 * j + 1],
+                   r[4 * j + 2], r[4 * j + 3]);
+        });
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_vempty + 8 * s);
+      }
+      {
+        const uint32_t prow = sb + L::kP + tt * 128;
+#pragma unroll
+        for (int c = 0; c < NH; c += 8) {
+          const int nh = NH * h + c, nl = N + NH * h + c;  // first column of the 16-byte chunk
+          sts128(prow + (nh >> 6) * 16384 + ((((nh & 63) >> 3) ^ (tt & 7)) << 4), hw[c / 2], hw[c / 2 + 1],
+                 hw[c / 2 + 2], hw[c / 2 + 3]);
+          sts128(prow + (nl >> 6) * 16384 + ((((nl & 63) >> 3) ^ (tt & 7)) << 4), lw[c / 2], lw[c / 2 + 1],
+                 lw[c / 2 + 2], lw[c / 2 + 3]);
         }
       }
+      fence_proxy_async_smem();  // V and P are read by the tensor core
       tc::wait_st();
-      fence_proxy_async_smem();
       tc::fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pv);
@@ -493,7 +520,7 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       p.partial_ml[base * 2 + 0] = mref_s[r];
       p.partial_ml[base * 2 + 1] = have_o ? l : 0.f;
     }
-    const int d = vt_lane_d(32 * q + lane, h);
+    const int d = 128 * h + tt;  // O^T lane tt of M half h
 #pragma unroll
     for (int c0 = 0; c0 < N; c0 += 8) {
       uint32_t hi[8], lo[8];
@@ -526,7 +553,7 @@ template <typename T, int N>
 cudaError_t launch_verify_tc_n(const SplitParams& p, cudaStream_t stream) {
   using L = VtLayout<N>;
   static_assert(L::kBytes <= 227 * 1024, "shared memory");
-  static_assert(kTmO + 4 * N <= kTmCols, "tensor memory columns");
+  static_assert(kTmO + 4 * N <= kTmCols && kTmS + 64 + N <= kTmO, "tensor memory columns");
   auto kernel = nvfp4_verify_tc_kernel<T, N>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
   if (e != cudaSuccess) return e;

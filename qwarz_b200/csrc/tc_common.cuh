@@ -99,10 +99,25 @@ QWZ_DEVINL uint64_t smem_desc_k128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory operand, MN-major with the 128-byte swizzle: rows of 128 B
+// hold 64 f16 of M (or N) for one K index; 8 K rows form a 1 KB atom.
+// lbo = byte distance between atoms along M/N (the next 64 elements), sbo =
+// byte distance between atoms along K (the next 8 K rows).
+QWZ_DEVINL uint64_t smem_desc_mn128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
 // Instruction descriptor of tcgen05.mma kind::f16: F16 A and B, F32
-// accumulator, both K-major, M x N.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
-  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// accumulator, M x N; A and B K-major unless a_mn_major / b_mn_major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major = false,
+                                                     bool a_mn_major = false) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // ------------------------------------------------------------------- MMA
