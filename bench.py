@@ -212,6 +212,7 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
     torch.cuda.synchronize()
 
     splits = ops.default_splits(device, local_tokens, 1)
+    exchange = None
     if world == 1:
         po, pml = ops.split_workspace(device, 1, splits)
 
@@ -225,7 +226,8 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
                 cache, perm = layers[l]
                 ops.attn_split(q[l], cache[0], cache[1], perm, pre, po, pml, cache[2], cache[3], splits)
     else:
-        dec = sharded.ShardedDecode(shard, device, 1, splits)
+        dec = sharded.ShardedDecode(shard, device, 1, splits, exchange=args.exchange)
+        exchange = dec.exchange
 
         def step():
             for l in range(LAYERS):
@@ -312,6 +314,10 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms_step, split_ms_launch, e2e_ms = float(t[0]), float(t[1]), float(t[2])
     del graph, split_graph
+    if world > 1:
+        torch.cuda.synchronize()
+        barrier()  # every rank is done with the peer buffers before any rank frees its own
+        dec.close()
     if rank != 0:
         return None
 
@@ -345,8 +351,9 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
                          "(256 pages of 256, seed-permuted tables), GQA 24/4 x 256"
                          if world == 1 else
                          f"weak-scaled C4: decode q_len=1, 16 layers x {tokens_total} tokens "
-                         f"sharded over {world} GPUs ({TOKENS_PER_GPU} per GPU), NCCL all-gather "
-                         "of (m,l,O) + LSE combine"),
+                         f"sharded over {world} GPUs ({TOKENS_PER_GPU} per GPU), (m,l,O) records "
+                         + ("exchanged over NVLink peer memory inside the merge kernel"
+                            if exchange == "peer" else "all-gathered by NCCL") + " + LSE combine"),
             "layers": LAYERS, "context_tokens": tokens_total, "tokens_per_gpu": local_tokens,
             "q_len": 1, "heads": "24q/4kv", "head_dim": DIM, "page": PAGE, "splits_per_head": splits,
             "l2": "inputs larger than L2: 16 layers x 75.5 MB KV rotate per step",
@@ -371,14 +378,14 @@ def run_ours(args, rank: int, world: int, device) -> dict | None:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "api": ("qwz_nvfp4_attend (C ABI, via qwarz_b200.ops.nvfp4_attend) per layer" if world == 1 else
-                    "qwarz_b200.sharded.ShardedDecode.step per layer (NCCL all-gather inside)")
+                    f"qwarz_b200.sharded.ShardedDecode.step per layer ({exchange} exchange inside)")
                    + "; one pinned H2D of the step's q/k/v and one D2H of its outputs; "
                      "captured in one CUDA graph, max over ranks",
         },
         # our kernels per timed step: split with fused append + combine (N=1);
         # append, split, partial combine, gathered combine (N>1); plus the
         # split-only roofline graph
-        "gpu_launches": args.steps * LAYERS * (2 if world == 1 else 4) + args.steps * LAYERS,
+        "gpu_launches": args.steps * LAYERS * (2 if world == 1 or exchange == "peer" else 4) + args.steps * LAYERS,
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -602,6 +609,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "peer", "nccl"],
+                    help="N>1: exchange of the shard records (auto: NVLink peer memory when every "
+                         "rank can reach every GPU, else NCCL)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="auto",
                     choices=["auto", "c3", "c4", "c5", "all", "profile_decode", "profile_verify",

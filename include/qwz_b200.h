@@ -174,6 +174,62 @@ int qwz_lse_combine_gathered(const float* gathered, void* out, int32_t world, in
                              int32_t dtype, void* stream);
 
 /*
+ * Sequence-sharded decode over NVLink peer memory (no reference
+ * counterpart: the reference is single-GPU).  Each rank owns one exchange
+ * buffer of qwz_peer_buffer_bytes(world, q_len) bytes, layout
+ *   uint64 [2 (epoch parity), world, q_len * 24, 258], each word an FP32
+ *   value (low half) tagged with the epoch of the call that wrote it,
+ * allocated zeroed by qwz_peer_alloc, which also returns its 64-byte CUDA
+ * IPC handle; the caller exchanges the handles (e.g. torch.distributed) and
+ * maps the other ranks' buffers with qwz_peer_open.  These set-up calls
+ * allocate and synchronise (once per rank); the per-step calls below do not.
+ */
+int64_t qwz_peer_buffer_bytes(int32_t world, int32_t q_len);  /* 0 when out of range */
+int qwz_peer_alloc(int64_t bytes, void** dev_ptr, uint8_t* ipc_handle);
+int qwz_peer_open(const uint8_t* ipc_handle, void** dev_ptr);
+int qwz_peer_close(void* peer_ptr);  /* a mapping from qwz_peer_open */
+int qwz_peer_free(void* dev_ptr);    /* the rank's own buffer */
+
+/*
+ * Shard split with the new rows appended: the split half of
+ * qwz_attn_shard_partial (local partials in partial_o / partial_ml) plus
+ * k, v [q_len, 4, 256] of the new rows, stored only by the rank whose pages
+ * hold them (inside the decode kernel at q_len 1).
+ */
+int qwz_attn_shard_split(const void* q, const void* k, const void* v, void* k_cache, void* v_cache,
+                         void* k_scales, void* v_scales, const int32_t* block_table,
+                         const int32_t* cache_seqlens, float* partial_o, float* partial_ml,
+                         int32_t table_width, int32_t num_pages, int32_t tok_begin, int32_t tok_span,
+                         int32_t q_len, int32_t num_splits, float sm_scale, int32_t dtype, void* stream);
+
+/*
+ * Exchange and merge in one kernel: merges this rank's num_splits partials
+ * into one (m, l, O) record per query row, stores it into every rank's
+ * buffer, raises the row's flag there and, once every rank's record is in
+ * (bounded wait; a timeout sets QWZ_DEVERR_TIMEOUT), LSE-merges them in rank
+ * order into out [q_len, 24, 256] FP16/BF16 (the same on every rank).
+ *   peers   HOST array [world] of the buffers' device addresses as this GPU
+ *           maps them (its own buffer at [rank])
+ *   epochs  device uint32 [q_len * 24], zeroed once; the kernel counts calls
+ * Every rank must call it the same number of times, with the same q_len.
+ */
+int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, int32_t num_splits,
+                               int32_t q_len, const uint64_t* peers, uint32_t* epochs, int32_t rank,
+                               int32_t world, void* out, int32_t dtype, void* stream);
+
+/*
+ * The same for `world` ranks emulated on one GPU in one cooperative launch
+ * (rank g's partials at partial_o + g * q_len*24*rank_stride_splits*256 and
+ * partial_ml + g * q_len*24*rank_stride_splits*2, its epochs at
+ * epochs + g * q_len*24, its output at out + g * q_len*24*256 elements;
+ * peers[g] = rank g's buffer on this GPU).
+ */
+int qwz_shard_exchange_combine_emulated(const float* partial_o, const float* partial_ml,
+                                        int64_t rank_stride_splits, int32_t num_splits, int32_t q_len,
+                                        const uint64_t* peers, uint32_t* epochs, void* out,
+                                        int32_t world, int32_t dtype, void* stream);
+
+/*
  * FP8 shadow-KV draft decode (replaces DecodeAttention.attend,
  * engine/forward/draft_attention.py:93-108): one query row per head,
  *   q      FP16 [1, 1, 24, 256]

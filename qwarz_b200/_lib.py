@@ -7,7 +7,7 @@ if the library is missing or fails to load, every operator raises.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, c_int32, c_void_p, c_char_p, POINTER
+from ctypes import c_float, c_int32, c_int64, c_void_p, c_char_p, POINTER
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libqwz_b200.so"
@@ -37,8 +37,18 @@ SIGNATURES = {
     "qwz_fp8_draft_decode": [c_void_p] * 9 + [c_int32, c_int32, c_void_p],
     "qwz_fp8_shadow_write": [c_void_p] * 7 + [c_int32, c_int32, c_void_p],
     "qwz_nvfp4_gather": [c_void_p] * 5 + [c_int32] * 6 + [c_void_p],
+    "qwz_peer_buffer_bytes": [c_int32, c_int32],
+    "qwz_peer_alloc": [c_int64, POINTER(c_void_p), c_void_p],
+    "qwz_peer_open": [c_void_p, POINTER(c_void_p)],
+    "qwz_peer_close": [c_void_p],
+    "qwz_peer_free": [c_void_p],
+    "qwz_attn_shard_split": [c_void_p] * 11 + [c_int32] * 6 + [c_float, c_int32, c_void_p],
+    "qwz_shard_exchange_combine": [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                                   c_int32, c_int32, c_void_p, c_int32, c_void_p],
+    "qwz_shard_exchange_combine_emulated": [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p,
+                                            c_void_p, c_void_p, c_int32, c_int32, c_void_p],
 }
-_RESTYPE = {"qwz_version": c_char_p, "qwz_last_error": c_char_p}
+_RESTYPE = {"qwz_version": c_char_p, "qwz_last_error": c_char_p, "qwz_peer_buffer_bytes": c_int64}
 
 _LIB = None
 

@@ -1,6 +1,7 @@
 // extern "C" entry points declared in include/qwz_b200.h: argument checks,
 // launch-parameter packing, error reporting.  Nothing here allocates device
-// memory or synchronises (except qwz_device_error, a diagnostic).
+// memory or synchronises, except qwz_device_error (a diagnostic) and the
+// peer-buffer set-up calls of the sharded decode (qwz_peer_*, once per rank).
 
 #include "qwz_common.cuh"
 #include "qwz_kernels.h"
@@ -10,6 +11,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -449,6 +451,139 @@ int qwz_nvfp4_gather(const void* packed, const void* scales, const int32_t* bloc
   p.head_dim = head_dim;
   p.page_size = page_size;
   return launched(qwz::launch_nvfp4_gather(p, as_stream(stream)), "qwz_nvfp4_gather");
+}
+
+
+// ------------------------------------------------ sharded decode over NVLink
+int64_t qwz_peer_buffer_bytes(int32_t world, int32_t q_len) {
+  if (world < 1 || world > qwz::kMaxWorld || q_len < 1 || q_len > 8) return 0;
+  const int64_t rows = (int64_t)q_len * qwz::kQHeads;
+  return 2 * (int64_t)world * rows * (qwz::kHeadDim + 2) * 8;  // two epoch-parity halves of tagged words
+}
+
+int qwz_peer_alloc(int64_t bytes, void** dev_ptr, uint8_t* ipc_handle) {
+  if (bytes <= 0 || !dev_ptr || !ipc_handle) return fail(QWZ_EINVAL, "bytes > 0, dev_ptr and ipc_handle are required");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return launched(e, "qwz_peer_alloc");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return QWZ_OK;
+}
+
+int qwz_peer_open(const uint8_t* ipc_handle, void** dev_ptr) {
+  if (!ipc_handle || !dev_ptr) return fail(QWZ_EINVAL, "ipc_handle and dev_ptr are required");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return launched(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "qwz_peer_open");
+}
+
+int qwz_peer_close(void* peer_ptr) {
+  if (!peer_ptr) return fail(QWZ_EINVAL, "peer_ptr is null");
+  return launched(cudaIpcCloseMemHandle(peer_ptr), "qwz_peer_close");
+}
+
+int qwz_peer_free(void* dev_ptr) {
+  if (!dev_ptr) return fail(QWZ_EINVAL, "dev_ptr is null");
+  return launched(cudaFree(dev_ptr), "qwz_peer_free");
+}
+
+int qwz_attn_shard_split(const void* q, const void* k, const void* v, void* k_cache, void* v_cache,
+                         void* k_scales, void* v_scales, const int32_t* block_table,
+                         const int32_t* cache_seqlens, float* partial_o, float* partial_ml,
+                         int32_t table_width, int32_t num_pages, int32_t tok_begin, int32_t tok_span,
+                         int32_t q_len, int32_t num_splits, float sm_scale, int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (tok_begin < 0 || tok_begin % qwz::kPage != 0) return fail(QWZ_EINVAL, "tok_begin must be a non-negative multiple of 256");
+  if (tok_span <= 0) return fail(QWZ_EINVAL, "tok_span must be positive");
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
+    return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+  qwz::SplitParams p;
+  rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens, partial_o,
+                  partial_ml, table_width, num_pages, q_len, num_splits, 0, sm_scale);
+  if (rc) return rc;
+  p.tok_begin = tok_begin;
+  p.tok_span = tok_span;
+  p.table_page_offset = tok_begin / qwz::kPage;
+  if (q_len == 1) {  // the shard that owns the new row's page writes it inside the decode kernel
+    p.app_k = k;
+    p.app_v = v;
+  } else {
+    rc = qwz_nvfp4_append_shard(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                                table_width, tok_begin / qwz::kPage, q_len, num_pages, dtype, stream);
+    if (rc) return rc;
+  }
+  return launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_attn_shard_split");
+}
+
+namespace {
+int fill_exchange(qwz::ExchangeParams& x, int32_t num_splits, int32_t q_len, const uint64_t* peers,
+                  int32_t world) {
+  if (world < 1 || world > qwz::kMaxWorld) return fail(QWZ_EINVAL, "world must be in 1..8");
+  if (q_len < 1 || q_len > 8) return fail(QWZ_EINVAL, "q_len must be in 1..8");
+  if (num_splits < 1 || num_splits > 65535) return fail(QWZ_EINVAL, "num_splits must be in 1..65535");
+  if (!peers) return fail(QWZ_EINVAL, "peers (host array of buffer addresses) is required");
+  x = qwz::ExchangeParams{};
+  for (int g = 0; g < world; ++g) {
+    if (!peers[g] || peers[g] % 16) return fail(QWZ_EINVAL, "every peer buffer address must be non-null and 16-byte aligned");
+    x.peers[g] = peers[g];
+  }
+  x.num_splits = num_splits;
+  x.rows = q_len * qwz::kQHeads;
+  x.world = world;
+  return QWZ_OK;
+}
+}  // namespace
+
+int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, int32_t num_splits,
+                               int32_t q_len, const uint64_t* peers, uint32_t* epochs, int32_t rank,
+                               int32_t world, void* out, int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!partial_o || !partial_ml || !epochs || !out) return fail(QWZ_EINVAL, "partials, epochs and out are required");
+  qwz::ExchangeParams x;
+  rc = fill_exchange(x, num_splits, q_len, peers, world);
+  if (rc) return rc;
+  if (rank < 0 || rank >= world) return fail(QWZ_EINVAL, "rank must be in 0..world-1");
+  x.po[0] = partial_o;
+  x.pml[0] = partial_ml;
+  x.epochs[0] = epochs;
+  x.out[0] = out;
+  x.rank0 = rank;
+  return launched(qwz::launch_shard_exchange(x, 0, dtype, as_stream(stream)), "qwz_shard_exchange_combine");
+}
+
+int qwz_shard_exchange_combine_emulated(const float* partial_o, const float* partial_ml,
+                                        int64_t rank_stride_splits, int32_t num_splits, int32_t q_len,
+                                        const uint64_t* peers, uint32_t* epochs, void* out,
+                                        int32_t world, int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!partial_o || !partial_ml || !epochs || !out) return fail(QWZ_EINVAL, "partials, epochs and out are required");
+  qwz::ExchangeParams x;
+  rc = fill_exchange(x, num_splits, q_len, peers, world);
+  if (rc) return rc;
+  if (rank_stride_splits < num_splits) return fail(QWZ_EINVAL, "rank_stride_splits must be >= num_splits");
+  const int64_t rows = (int64_t)q_len * qwz::kQHeads;
+  const size_t esize = 2;  // FP16 / BF16
+  for (int g = 0; g < world; ++g) {
+    x.po[g] = partial_o + (size_t)g * rows * rank_stride_splits * qwz::kHeadDim;
+    x.pml[g] = partial_ml + (size_t)g * rows * rank_stride_splits * 2;
+    x.epochs[g] = epochs + (size_t)g * rows;
+    x.out[g] = static_cast<uint8_t*>(out) + (size_t)g * rows * qwz::kHeadDim * esize;
+  }
+  x.rank0 = 0;
+  return launched(qwz::launch_shard_exchange(x, 1, dtype, as_stream(stream)),
+                  "qwz_shard_exchange_combine_emulated");
 }
 
 }  // extern "C"

@@ -5,6 +5,7 @@
 #include "attn_split.cu"
 #include "attn_draft.cu"
 #include "attn_combine.cu"
+#include "shard_exchange.cu"
 #include "kv_write.cu"
 #include "capi.cu"
 #include "noalloc.cu"

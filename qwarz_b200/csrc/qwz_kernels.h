@@ -98,7 +98,24 @@ struct GatherParams {
   int batch, max_tokens, table_width, n_heads, head_dim, page_size;
 };
 
+// Sequence-sharded decode: record exchange over peer memory + final merge.
+// Arrays are indexed by blockIdx.y (emulated ranks on one GPU) or hold one
+// entry (a real rank, rank0 = its rank).
+constexpr int kMaxWorld = 8;
+struct ExchangeParams {
+  const float* po[kMaxWorld];    // [rows, num_splits, 256] split partials of the rank
+  const float* pml[kMaxWorld];   // [rows, num_splits, 2]
+  uint32_t* epochs[kMaxWorld];   // [rows] call counters of the rank
+  void* out[kMaxWorld];          // [rows, 256] FP16/BF16
+  uint64_t peers[kMaxWorld];     // exchange buffer of every rank, as this GPU addresses it
+  int num_splits;
+  int rows;
+  int world;
+  int rank0;
+};
+
 cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_shard_exchange(const ExchangeParams& p, int emulated, int dtype, cudaStream_t stream);
 cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStream_t stream);
 cudaError_t launch_nvfp4_append(const AppendParams& p, int dtype, cudaStream_t stream);

@@ -1,0 +1,184 @@
+// Sequence-sharded decode: the record exchange and the final LSE merge fused
+// into one kernel over NVLink peer memory (no reference counterpart; the
+// reference is single-GPU, src/qwasar_runtime/engine.py:602-610).
+//
+// Every rank owns an exchange buffer of identical layout:
+//   records u64 [2][world][rows][258]: (m, l, O[256]) of rank src at
+//   [e & 1][src], each value in the low 32 bits of a word whose high 32 bits
+//   carry the epoch e of the call that wrote it.  Alternating halves by
+//   epoch parity means a rank that runs ahead to call e+1 never overwrites a
+//   call-e record a slower rank has yet to read (reaching call e+2 needs the
+//   slower rank's call-e+1 record, written after its call e finished).
+// A 64-bit aligned store reaches the peer as one unit, so the value and its
+// epoch arrive together and the reader polls the data itself: there is no
+// separate flag and no system-scope fence (the low-latency protocol of small
+// collectives).  CTA r of rank g:
+//   1. merges rank g's num_splits partials of row r (split order fixed) into
+//      one (m, l, O) record;
+//   2. stores it, tagged with e = this row's call count, into every rank's
+//      buffer at [g][r] (stores into the peers' memory);
+//   3. reads the world records of row r from its own buffer, waiting per
+//      word until it carries epoch e (bounded by globaltimer: a timeout sets
+//      kErrTimeout and merges what is there), and merges them in rank order,
+//      so every rank writes the same output.
+// Epochs count calls per row on every rank (a device word per row, advanced
+// by the kernel), so repeated launches and CUDA-graph replays need no reset.
+// With fewer GPUs than ranks the kernel runs all ranks in one cooperative
+// launch (blockIdx.y = rank, buffers on one GPU), so ranks that wait on one
+// another are always co-resident.
+
+#include "qwz_common.cuh"
+#include "qwz_kernels.h"
+
+#include <math_constants.h>
+
+namespace qwz {
+
+namespace {
+
+constexpr uint64_t kExchangeTimeoutNs = 500ull * 1000 * 1000;  // 0.5 s
+constexpr int kRecWords = kHeadDim + 2;                         // m, l, O[256]
+
+QWZ_DEVINL uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+QWZ_DEVINL void st_tagged(uint64_t* p, float v, uint32_t e) {
+  const uint64_t w = (uint64_t)__float_as_uint(v) | ((uint64_t)e << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+QWZ_DEVINL uint64_t ld_tagged(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// The value of a tagged word once it carries epoch e; false on timeout.
+QWZ_DEVINL bool wait_tagged(const uint64_t* p, uint32_t e, uint64_t t0, float& v) {
+  for (int i = 0;; ++i) {
+    const uint64_t w = ld_tagged(p);
+    if ((uint32_t)(w >> 32) == e) {
+      v = __uint_as_float((uint32_t)w);
+      return true;
+    }
+    if ((i & 63) == 63) {
+      if (global_ns() - t0 > kExchangeTimeoutNs) {
+        v = __uint_as_float((uint32_t)w);
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+}
+
+}  // namespace
+
+template <typename TOut>
+__global__ void __launch_bounds__(256) shard_exchange_kernel(const ExchangeParams p) {
+  constexpr int GROUPS = 8;
+  __shared__ float red_o[GROUPS][kHeadDim];
+  __shared__ float red_l[GROUPS];
+  __shared__ float red_m[GROUPS];
+  __shared__ uint32_t s_epoch;
+  const int r = blockIdx.x, y = blockIdx.y, rank = p.rank0 + y;
+  const int tid = threadIdx.x, grp = tid >> 5, lane = tid & 31;
+  const int S = p.num_splits, rows = p.rows;
+
+  // ---------------------------------------------- 1. this rank's record
+  const float* ml = p.pml[y] + (size_t)r * S * 2;
+  const float* po = p.po[y] + (size_t)r * S * kHeadDim + lane * 8;
+  float M = -CUDART_INF_F;
+  for (int s = tid; s < S; s += 256) M = fmaxf(M, ml[2 * s]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red_m[grp] = M;
+  if (tid == 0) s_epoch = p.epochs[y][r] + 1u;
+  __syncthreads();
+  M = red_m[0];
+#pragma unroll
+  for (int i = 1; i < GROUPS; ++i) M = fmaxf(M, red_m[i]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float ls = 0.f;
+  if (M != -CUDART_INF_F) {
+#pragma unroll 4
+    for (int s = grp; s < S; s += GROUPS) {  // empty splits (m = -inf, O = 0) weigh 0
+      const float m = ml[2 * s];
+      const float w = m == -CUDART_INF_F ? 0.f : exp2_approx(m - M);
+      ls += w * ml[2 * s + 1];
+      const float4 a = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim);
+      const float4 b = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim + 4);
+      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+      acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red_o[grp][lane * 8 + i] = acc[i];
+  if (lane == 0) red_l[grp] = ls;
+  __syncthreads();
+  float o = 0.f, L = 0.f;
+#pragma unroll
+  for (int i = 0; i < GROUPS; ++i) {
+    o += red_o[i][tid];
+    L += red_l[i];
+  }
+  const uint32_t e = s_epoch;
+
+  // ------------------------------------------- 2. store it on every rank
+  const size_t half = (size_t)(e & 1u) * p.world * rows * kRecWords;
+  const size_t rec = half + ((size_t)rank * rows + r) * kRecWords;
+  for (int g = 0; g < p.world; ++g) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.peers[g]) + rec;
+    st_tagged(dst + 2 + tid, o, e);
+    if (tid == 0) {
+      st_tagged(dst, M, e);
+      st_tagged(dst + 1, L, e);
+    }
+  }
+
+  // --------------------------------------- 3. wait for all, merge, write
+  const uint64_t* local = reinterpret_cast<const uint64_t*>(p.peers[rank]);
+  const uint64_t t0 = global_ns();
+  bool ok = true;
+  float mg[kMaxWorld], lg[kMaxWorld], og[kMaxWorld];
+#pragma unroll
+  for (int g = 0; g < kMaxWorld; ++g) {
+    mg[g] = -CUDART_INF_F;
+    lg[g] = og[g] = 0.f;
+    if (g < p.world) {
+      const uint64_t* src = local + half + ((size_t)g * rows + r) * kRecWords;
+      ok &= wait_tagged(src, e, t0, mg[g]);
+      ok &= wait_tagged(src + 1, e, t0, lg[g]);
+      ok &= wait_tagged(src + 2 + tid, e, t0, og[g]);
+    }
+  }
+  if (!ok) flag_error(kErrTimeout);
+  float Mg = -CUDART_INF_F;
+#pragma unroll
+  for (int g = 0; g < kMaxWorld; ++g) Mg = fmaxf(Mg, mg[g]);
+  float on = 0.f, ln = 0.f;
+  if (Mg != -CUDART_INF_F) {
+#pragma unroll
+    for (int g = 0; g < kMaxWorld; ++g) {
+      if (g >= p.world || mg[g] == -CUDART_INF_F) continue;
+      const float w = exp2_approx(mg[g] - Mg);
+      ln += w * lg[g];
+      on += w * og[g];
+    }
+  }
+  TOut* out = reinterpret_cast<TOut*>(p.out[y]) + (size_t)r * kHeadDim;
+  out[tid] = InTraits<TOut>::from_float(ln > 0.f ? on / ln : 0.f);
+  if (tid == 0) p.epochs[y][r] = e;
+}
+
+cudaError_t launch_shard_exchange(const ExchangeParams& p, int emulated, int dtype, cudaStream_t stream) {
+  if (p.rows <= 0) return cudaSuccess;
+  dim3 grid(p.rows, emulated ? p.world : 1);
+  void* args[] = {const_cast<ExchangeParams*>(&p)};
+  auto kernel = dtype == kDtypeBF16 ? (const void*)shard_exchange_kernel<__nv_bfloat16>
+                                    : (const void*)shard_exchange_kernel<__half>;
+  if (emulated)  // ranks that wait on one another must be co-resident
+    return cudaLaunchCooperativeKernel(kernel, grid, dim3(256), args, 0, stream);
+  return cudaLaunchKernel(kernel, grid, dim3(256), args, 0, stream);
+}
+
+}  // namespace qwz

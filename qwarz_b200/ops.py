@@ -8,6 +8,8 @@ missing library raises.
 """
 from __future__ import annotations
 
+import ctypes
+
 import math
 
 import torch
@@ -230,6 +232,57 @@ def shard_partial(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_se
         _p(cache_seqlens), _p(partial_o), _p(partial_ml), _p(send_buf), block_table.shape[-1], P,
         tok_begin, tok_span, q_len, num_splits, float(sm_scale), _dtype_code(q.dtype),
         _stream(dev)), "qwz_attn_shard_partial")
+
+
+def shard_split(q, k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
+                partial_o, partial_ml, tok_begin: int, tok_span: int, num_splits: int,
+                sm_scale: float = DIM ** -0.5) -> None:
+    """Shard split with the new rows appended (only the owning shard stores them)."""
+    dev = _cuda(q, k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens, partial_o,
+                partial_ml)
+    P = check_cache(k_cache, v_cache, k_scales, v_scales)
+    _check_lengths(block_table, cache_seqlens)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _contig(name, t)
+    q_len = q.numel() // (HEADS * DIM)
+    if k.numel() != q_len * KV_HEADS * DIM or v.numel() != k.numel():
+        raise ValueError("k and v must hold q_len rows [q_len, 4, 256]")
+    if partial_o.numel() < q_len * HEADS * num_splits * DIM or partial_ml.numel() < q_len * HEADS * num_splits * 2:
+        raise ValueError("split workspace too small for num_splits")
+    lib = _lib.load()
+    _lib.check(lib.qwz_attn_shard_split(
+        _p(q), _p(k), _p(v), _p(k_cache), _p(v_cache), _p(k_scales), _p(v_scales), _p(block_table),
+        _p(cache_seqlens), _p(partial_o), _p(partial_ml), block_table.shape[-1], P, tok_begin, tok_span,
+        q_len, num_splits, float(sm_scale), _dtype_code(q.dtype), _stream(dev)), "qwz_attn_shard_split")
+
+
+def shard_exchange_combine(partial_o, partial_ml, num_splits: int, peers, epochs, rank: int, world: int,
+                           out) -> None:
+    """Merge this rank's splits, exchange the records over peer memory and merge
+    all ranks' records into out; `peers` is a ctypes uint64 array of the
+    ranks' exchange buffers as this GPU maps them."""
+    dev = _cuda(partial_o, partial_ml, epochs, out)
+    q_len = out.numel() // (HEADS * DIM)
+    if epochs.dtype != torch.int32 or epochs.numel() < q_len * HEADS:
+        raise ValueError("epochs must be int32 with q_len*24 elements")
+    lib = _lib.load()
+    _lib.check(lib.qwz_shard_exchange_combine(
+        _p(partial_o), _p(partial_ml), num_splits, q_len, ctypes.cast(peers, ctypes.c_void_p), _p(epochs),
+        rank, world, _p(out), _dtype_code(out.dtype), _stream(dev)), "qwz_shard_exchange_combine")
+
+
+def shard_exchange_combine_emulated(partial_o, partial_ml, num_splits: int, peers, epochs, out) -> None:
+    """All ranks on one GPU (one cooperative launch): partial_o [world, rows,
+    splits, 256], partial_ml [world, rows, splits, 2], epochs int32
+    [world, rows], out [world, rows, 256]; peers[g] = rank g's buffer."""
+    dev = _cuda(partial_o, partial_ml, epochs, out)
+    world = partial_o.shape[0]
+    q_len = out[0].numel() // (HEADS * DIM)
+    lib = _lib.load()
+    _lib.check(lib.qwz_shard_exchange_combine_emulated(
+        _p(partial_o), _p(partial_ml), partial_o.shape[2], num_splits, q_len,
+        ctypes.cast(peers, ctypes.c_void_p), _p(epochs), _p(out), world, _dtype_code(out.dtype),
+        _stream(dev)), "qwz_shard_exchange_combine_emulated")
 
 
 def combine_gathered(gathered, out, world: int) -> None:

@@ -15,17 +15,24 @@ block table whose entry 0 is its first page.  Q is replicated.  Each call:
   4. combine  — every rank LSE-merges the G records in rank order, so the
                 output is replicated and identical on all ranks.
 
+With exchange="peer" (the default for NCCL groups on one node) steps 1-2
+are one launch (the owning shard appends inside its split kernel) and steps
+2b-4 are one kernel over NVLink peer memory (qwz_shard_exchange_combine):
+each rank writes its records straight into every rank's exchange buffer
+(mapped with CUDA IPC) and merges once all have arrived.
+
 `exchange_records` also runs on gloo CPU tensors, which the host-logic tests
 use with oracle-computed records.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 PAGE = 256
 RECORD = ops.RECORD
@@ -77,12 +84,64 @@ def exchange_records(send: torch.Tensor, gathered: torch.Tensor, group=None) -> 
     return gathered
 
 
+class PeerExchange:
+    """Every rank's exchange buffer mapped on this GPU (CUDA IPC), plus this
+    rank's per-row call counters, for qwz_shard_exchange_combine.  Collective:
+    every rank of `group` constructs it together."""
+
+    def __init__(self, world: int, rank: int, q_len: int, device, group=None):
+        lib = _lib.load()
+        self.device = torch.device(device)
+        nbytes = lib.qwz_peer_buffer_bytes(world, q_len)
+        if nbytes <= 0:
+            raise ValueError("world must be 1..8 and q_len 1..8")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.qwz_peer_alloc(nbytes, ctypes.byref(own), handle), "qwz_peer_alloc")
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self._own = own.value
+            self._opened = []
+            addrs = []
+            for g in range(world):
+                if g == rank:
+                    addrs.append(own.value)
+                    continue
+                ptr = ctypes.c_void_p()
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[g])
+                _lib.check(lib.qwz_peer_open(buf, ctypes.byref(ptr)), "qwz_peer_open")
+                self._opened.append(ptr.value)
+                addrs.append(ptr.value)
+        self.peers = (ctypes.c_uint64 * world)(*addrs)
+        self.epochs = torch.zeros(q_len * HEADS, dtype=torch.int32, device=self.device)
+
+    def close(self) -> None:
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                lib.qwz_peer_close(ctypes.c_void_p(ptr))
+            self._opened = []
+            if self._own:
+                lib.qwz_peer_free(ctypes.c_void_p(self._own))
+                self._own = None
+
+
+def _peer_capable(device, world: int, group) -> bool:
+    if world < 2 or world > 8 or dist.get_backend(group) != "nccl":
+        return False
+    here = torch.device(device).index
+    n = torch.cuda.device_count()
+    return n >= world and all(torch.cuda.can_device_access_peer(here, g) for g in range(n) if g != here)
+
+
 class ShardedDecode:
     """One rank's side of the sharded decode; buffers are allocated once, so
-    `step` can be captured in a CUDA graph together with the NCCL call."""
+    `step` can be captured in a CUDA graph (with the NCCL call, or with the
+    peer-memory exchange kernel)."""
 
     def __init__(self, shard: Shard, device, q_len: int = 1, num_splits: int | None = None,
-                 group=None):
+                 group=None, exchange: str = "auto"):
         self.shard = shard
         self.device = torch.device(device)
         self.q_len = q_len
@@ -90,8 +149,19 @@ class ShardedDecode:
         self.splits = num_splits or ops.default_splits(self.device, shard.tok_span, q_len)
         self.partial_o, self.partial_ml = ops.split_workspace(self.device, q_len, self.splits)
         rows = q_len * HEADS
+        if exchange == "auto":
+            exchange = "peer" if _peer_capable(self.device, shard.world, group) else "nccl"
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'auto', 'peer' or 'nccl'")
+        self.exchange = exchange
+        self.peer = PeerExchange(shard.world, shard.rank, q_len, self.device, group) if exchange == "peer" else None
         self.send = torch.empty(rows, RECORD, dtype=torch.float32, device=self.device)
         self.gathered = torch.empty(shard.world, rows, RECORD, dtype=torch.float32, device=self.device)
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def append(self, k, v, cache, local_table, cache_seqlens) -> None:
         k_cache, v_cache, k_scales, v_scales = cache
@@ -108,6 +178,14 @@ class ShardedDecode:
              sm_scale: float = 256 ** -0.5) -> torch.Tensor:
         """Append the new rows, attend over the whole sharded sequence, return out
         (identical on every rank)."""
+        if self.peer is not None:
+            k_cache, v_cache, k_scales, v_scales = cache
+            ops.shard_split(q, k, v, k_cache, v_cache, k_scales, v_scales, local_table, cache_seqlens,
+                            self.partial_o, self.partial_ml, self.shard.tok_begin, self.shard.tok_span,
+                            self.splits, sm_scale)
+            ops.shard_exchange_combine(self.partial_o, self.partial_ml, self.splits, self.peer.peers,
+                                       self.peer.epochs, self.shard.rank, self.shard.world, out)
+            return out
         self.append(k, v, cache, local_table, cache_seqlens)
         self.partial(q, cache, local_table, cache_seqlens, sm_scale)
         exchange_records(self.send, self.gathered, self.group)

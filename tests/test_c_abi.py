@@ -22,7 +22,7 @@ def lib():
 
 def declared():
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(qwz_\w+)\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(qwz_\w+)\(", text, flags=re.M)))
 
 
 def test_header_declares_entry_points():
@@ -110,3 +110,27 @@ def test_python_ops_refuse_cpu_tensors():
         ops.attn_split(q, cache[0], cache[1], torch.zeros(1, 1, dtype=torch.int32),
                        torch.zeros(1, dtype=torch.int32), torch.zeros(1), torch.zeros(1),
                        cache[2], cache[3], 1)
+
+
+def test_peer_buffer_size_and_exchange_argument_checks(lib):
+    rows = 24
+    assert lib.qwz_peer_buffer_bytes(1, 1) == 2 * rows * 258 * 8
+    assert lib.qwz_peer_buffer_bytes(8, 2) == 2 * 8 * 2 * rows * 258 * 8
+    assert lib.qwz_peer_buffer_bytes(0, 1) == 0 and lib.qwz_peer_buffer_bytes(9, 1) == 0
+    assert lib.qwz_peer_buffer_bytes(2, 9) == 0
+    buf = ctypes.create_string_buffer(4096 + 64)
+    addr = (ctypes.addressof(buf) + 63) // 64 * 64
+    peers = (ctypes.c_uint64 * 2)(addr, addr)
+    pv = ctypes.cast(peers, ctypes.c_void_p)
+    for world, rank, q_len, splits, p, needle in [
+            (9, 0, 1, 4, pv, "world"), (2, 2, 1, 4, pv, "rank"), (2, 0, 0, 4, pv, "q_len"),
+            (2, 0, 1, 0, pv, "num_splits"), (2, 0, 1, 4, None, "peers")]:
+        rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine(addr, addr, splits, q_len, p, addr, rank,
+                                                                  world, addr, 0, None))
+        assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)
+    bad = (ctypes.c_uint64 * 2)(addr + 8, addr)
+    rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine(addr, addr, 4, 1, ctypes.cast(bad, ctypes.c_void_p),
+                                                              addr, 0, 2, addr, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "16-byte aligned" in msg
+    rc, msg = _rc_and_msg(lib, lib.qwz_attn_shard_split(*([addr] * 11), 4, 1, 100, 256, 1, 4, 0.0625, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "tok_begin" in msg

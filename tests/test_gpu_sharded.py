@@ -10,9 +10,10 @@ import pytest
 import torch
 
 from oracle import attention as oatt
-from oracle import rng
+from oracle import nvfp4, rng
 from qwarz_b200 import sharded
 from tests.conftest import assert_close_attention
+from tests.golden import cases
 from tests.gpu_helpers import make_cache, queries, to_cpu_torch, to_device
 
 pytestmark = pytest.mark.gpu
@@ -72,3 +73,66 @@ def test_shard_append_writes_only_the_owners_rows(cuda):
         assert written == (s.rank == sharded.owner(pre, shards)), s
     from qwarz_b200 import _lib
     assert _lib.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("world,total,dtype", [(2, 2000, torch.float16), (3, 1500, torch.float16),
+                                               (4, 4100, torch.bfloat16), (8, 8300, torch.float16)])
+def test_peer_exchange_emulated_ranks_match_full_attention(cuda, world, total, dtype):
+    """Every emulated rank runs the fused shard split (only the owner of the
+    new row's page appends it), then all ranks exchange their records through
+    peer-layout buffers in one cooperative launch.  Each rank's output must
+    match the oracle over the whole sequence and all ranks must agree
+    exactly; a second call (the next position) checks that the per-row
+    epochs advance; the shard pools must end up holding the oracle's bytes."""
+    import ctypes
+
+    from qwarz_b200 import _lib, ops
+
+    lib = _lib.load()
+    pages = max((total + 2 + 255) // 256, world)
+    table = rng.permutation(40 + world, pages)
+    c, _, _ = make_cache(800 + world, total, pages, table)
+    ref = {n: c[n].copy() for n in ("k_cache", "v_cache", "k_scales", "v_scales", "table")}
+    shards = sharded.shard_pages(pages, world)
+    local = []
+    for s in shards:
+        phys = table[s.first_page:s.first_page + s.num_pages]
+        d = {n: np.ascontiguousarray(c[n][phys]) for n in ("k_cache", "v_cache", "k_scales", "v_scales")}
+        d["table"] = np.arange(s.num_pages, dtype=np.int32)
+        local.append(to_device(d, cuda))
+    rows, splits = 24, 3
+    po = torch.empty(world, rows, splits, 256, dtype=torch.float32, device=cuda)
+    pml = torch.empty(world, rows, splits, 2, dtype=torch.float32, device=cuda)
+    bufs = [torch.zeros(lib.qwz_peer_buffer_bytes(world, 1), dtype=torch.uint8, device=cuda) for _ in range(world)]
+    peers = (ctypes.c_uint64 * world)(*[b.data_ptr() for b in bufs])
+    epochs = torch.zeros(world, rows, dtype=torch.int32, device=cuda)
+    out = torch.empty(world, rows, 256, dtype=dtype, device=cuda)
+    _lib.device_error(clear=True)
+    for step in range(2):
+        pre = total + step
+        q = queries(900 + 10 * world + step, 1, dtype)
+        kn = torch.from_numpy(cases.kv_rows(950 + step, 1)).to(dtype)
+        vn = torch.from_numpy(cases.kv_rows(960 + step, 1)).to(dtype)
+        nvfp4.append(kn.float().numpy(), vn.float().numpy(), ref["k_cache"], ref["v_cache"], ref["k_scales"],
+                      ref["v_scales"], table, pre)
+        lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+        qd, kd, vd = q.to(cuda), kn.to(cuda), vn.to(cuda)
+        for s in shards:
+            dc = local[s.rank]
+            ops.shard_split(qd, kd, vd, dc["k_cache"], dc["v_cache"], dc["k_scales"], dc["v_scales"],
+                            dc["table"], lens, po[s.rank], pml[s.rank], s.tok_begin, s.tok_span, splits)
+        ops.shard_exchange_combine_emulated(po, pml, splits, peers, epochs, out)
+        torch.cuda.synchronize()
+        expect = oatt.nvfp4_attention(q.float(), **{k: v for k, v in to_cpu_torch(ref).items() if k != "table"},
+                                      block_table=torch.from_numpy(table), pre_len=pre)
+        for g in range(world):
+            assert_close_attention(out[g].float().cpu().view(1, 24, 256).numpy(), expect.numpy(),
+                                   f"peer exchange world={world} rank={g} step={step}", str(dtype).split(".")[-1])
+            assert torch.equal(out[g], out[0]), f"rank {g} differs from rank 0"
+    assert (epochs == 2).all()
+    assert _lib.device_error(clear=True) == 0
+    for s in shards:
+        phys = table[s.first_page:s.first_page + s.num_pages]
+        for n in ("k_cache", "v_cache", "k_scales", "v_scales"):
+            got = local[s.rank][n].view(torch.uint8).cpu().numpy()
+            np.testing.assert_array_equal(got, ref[n][phys], err_msg=f"{n} shard {s.rank}")
