@@ -26,9 +26,10 @@ DECODE_POLICY = {
     "q1": {"kernel": "nvfp4_decode_kernel", "warps": 8, "stage_tokens": 256, "stages": 3,
            "copy": "TMA 2-D boxes, 128-byte swizzle", "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
            "ctas_per_sm": 1, "append": "fused when called through qwz_nvfp4_attend"},
-    "q2-8": {"kernel": "nvfp4_verify_tc_kernel", "warps": 10, "roles": "TMA, MMA/TMEM owner, 8 math",
-             "stage_tokens": 128, "stages": 4, "copy": "TMA 2-D boxes, 128-byte swizzle",
-             "mma": "tcgen05 kind::f16 M=128: S^T = K Q^T (N=16/32/48), O^T = V^T [P_hi|P_lo]^T (N=2x)",
+    "q2-8": {"kernel": "nvfp4_verify_tc_kernel", "warps": 19,
+             "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
+             "stage_tokens": 128, "stages": {"K": 3, "V": 2}, "copy": "TMA 2-D boxes, 128-byte swizzle",
+             "mma": "tcgen05 kind::f16 M=128: S^T = K Q^T (K from TMEM, N=16/32/48), O^T = V^T P^T (FP16 P)",
              "tmem_columns": 512, "ctas_per_sm": 1},
     "draft": {"kernel": "fp8_draft_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
               "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37},

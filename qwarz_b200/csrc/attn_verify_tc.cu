@@ -5,13 +5,16 @@
 // (MTP verify: q_len query rows per head, lower-right causal, xqa.py:662)
 // behind the split ABI of tests/test_attention_kernel_abi.py:13-32.
 //
-// CTA = one KV head x one split (a run of pages), 11 warps:
+// CTA = one KV head x one split (a run of pages), 19 warps:
 //   warp 0      TMA producer of K tiles (codes + scales, 18 KB per 128
 //               tokens) into a 3-deep ring;
 //   warp 1      TMEM owner (512 columns) and MMA issuer (one thread);
 //   warp 2      TMA producer of V tiles into a 2-deep ring;
-//   warps 3-10  eight math warps: warp w serves TMEM lane quadrant q = w % 4
-//               and half h = (w - 3) / 4 of the work.
+//   warps 3-18  sixteen math warps: warp w serves TMEM lane quadrant
+//               q = w % 4 and quarter u = (w - 3) / 4 of the work (a quarter
+//               of the head dim for K and V, of the score columns for the
+//               softmax), four warps per scheduler to hide the TMEM,
+//               shared-memory and barrier latencies.
 // Per 128-token tile i (tokens on the MMA M dimension, head-dim d):
 //   K(i)    math: E2M1 x E4M3 -> FP16 (exact) into TMEM as the A operand,
 //           lane = token, column = d pair (32x32b stores, thread = token);
@@ -19,19 +22,18 @@
 //           6 q_len rounded up to 16, Q in shared memory (K-major, 128-byte
 //           swizzle, rows scaled by a power of two so BF16 queries convert
 //           to FP16 exactly);
-//   soft(i) math: base-2 online softmax on S^T (thread = token): the
-//           reference max of a column only moves when a score exceeds it by
-//           kLazy (then O is rescaled in TMEM); P = hi + lo in FP16;
+//   soft(i) math: base-2 online softmax on S^T (thread = token, packed
+//           f32x2 arithmetic): the reference max of a column only moves when
+//           a score exceeds it by kLazy (then O is rescaled in TMEM); P in
+//           FP16, the PV operand precision of the reference's XQA kernel;
 //   V(i)    math: V -> FP16 rows [token][d] in shared memory (the MN-major A
-//           operand of PV), P -> [token][hi | lo] (the MN-major B operand);
-//   PV(i)   MMA:  O^T[256 d x 2N] += V^T [P_hi | P_lo]^T, two M=128 halves
-//           of d, V^T read once for both halves of P.
+//           operand of PV), P -> [token][N] (the MN-major B operand);
+//   PV(i)   MMA:  O^T[256 d x N] += V^T P^T, two M=128 halves of d.
 // Order: the math warps dequantise K(i+1) as soon as S(i) is read, so
 // QK(i+1) is queued ahead of PV(i); they write V(i) and P(i) only after
 // PV(i-1) has finished with the single V and P buffers, which by then it
-// long has.  The epilogue adds the hi and lo halves of O^T and writes one
-// (m, l, O) record per query row and split, the layout lse_combine_kernel
-// reads.  Every wait is bounded; the math warps decide timeouts
+// long has.  The epilogue writes one (m, l, O) record per query row and
+// split, the layout lse_combine_kernel reads.  Every wait is bounded; the math warps decide timeouts
 // collectively at a per-tile vote, so named barriers never wait for a warp
 // that left.
 
@@ -42,8 +44,14 @@ namespace qwz {
 
 using namespace detail;
 
-constexpr int kVtWarps = 11;
+#ifndef QWZ_VT_MATH_WARPS
+#define QWZ_VT_MATH_WARPS 16
+#endif
+constexpr int kVtMathWarps = QWZ_VT_MATH_WARPS;            // 8 or 16
 constexpr int kVtMath0 = 3;                                // first math warp
+constexpr int kVtWarps = kVtMath0 + kVtMathWarps;
+constexpr int kVtParts = kVtMathWarps / 4;                 // math warps per TMEM lane quadrant
+static_assert(kVtParts == 2 || kVtParts == 4, "8 or 16 math warps");
 constexpr int kVtKStages = 3, kVtVStages = 2;
 constexpr int kVtTile = 128;
 constexpr int kVtCodeBox = kVtTile * kCodeBytes;           // 16 KB
@@ -60,7 +68,7 @@ struct VtLayout {
   static constexpr int kVRing = kKRing + kVtKStages * kVtHalfStage;  // 2 x 18 KB
   static constexpr int kVf = 92160;                                  // V FP16: [2h+a][128 tok][128 B]
   static constexpr int kQ = kVf + 4 * 16384;                         // Q: 4 k-atoms [N x 128 B]
-  static constexpr int kPAtoms = (2 * N + 63) / 64;                  // P: n-atoms [128 tok][128 B]
+  static constexpr int kPAtoms = (N + 63) / 64;                      // P: n-atoms [128 tok][128 B]
   static constexpr int kP = kQ + N * 512;
   static constexpr int kBars = kP + kPAtoms * 16384;
   // kfull[3] kempty[3] vfull[2] vempty[2] kready pvready s[2] o (15 x 8 B)
@@ -68,7 +76,7 @@ struct VtLayout {
   static constexpr int kRowfac = kMeta + 32;                         // stage ends, tmem, abort, fin
   static constexpr int kAlpha = kRowfac + 4 * N;
   static constexpr int kMref = kAlpha + 4 * N;
-  static constexpr int kWred = kMref + 4 * N;                        // [2 h][4 q][N / 2]
+  static constexpr int kWred = kMref + 4 * N;                        // [parts][4 q][N / parts]
   static constexpr int kPid = kWred + 4 * 4 * N;
   static constexpr int kBytes = kPid + 4 * kVtPidCache + 1024;
   static_assert(kVRing + kVtVStages * kVtHalfStage <= kVf && kVf % 1024 == 0, "ring / V layout");
@@ -80,14 +88,16 @@ struct VtLayout {
 
 namespace {
 
-QWZ_DEVINL void math_bar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }
+// Named barrier 1: exactly the kVtMathWarps math warps take part.
+constexpr int kVtMathThreads = kVtMathWarps * 32;
+QWZ_DEVINL void math_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(kVtMathThreads) : "memory"); }
 QWZ_DEVINL bool math_bar_or(bool v) {
   uint32_t r;
   asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n"
       " selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"((uint32_t)v)
+      : "r"((uint32_t)v), "n"(kVtMathThreads)
       : "memory");
   return r != 0;
 }
@@ -110,10 +120,23 @@ QWZ_DEVINL float warp_sum(float v) {
   return v;
 }
 
+// tcgen05.ld writes its registers asynchronously; after tcgen05.wait::ld,
+// route them through an empty asm so no use is scheduled above the wait.
+template <int NC>
+QWZ_DEVINL void regs_ready(float (&v)[NC]) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) asm volatile("" : "+f"(v[c])::"memory");
+}
+template <int NC>
+QWZ_DEVINL void regs_ready(uint32_t (&v)[NC]) {
+#pragma unroll
+  for (int c = 0; c < NC; ++c) asm volatile("" : "+r"(v[c])::"memory");
+}
+
 // TMEM loads of NC (multiple of 8) consecutive columns into v.
 template <int NC>
 QWZ_DEVINL void ld_cols(uint32_t taddr, float (&v)[NC]) {
-  static_assert(NC % 8 == 0, "8-column granularity");
+  static_assert(NC % 4 == 0, "4-column granularity");
 #pragma unroll
   for (int c = 0; c + 16 <= NC; c += 16) {
     uint32_t r[16];
@@ -121,11 +144,43 @@ QWZ_DEVINL void ld_cols(uint32_t taddr, float (&v)[NC]) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[c + j] = __uint_as_float(r[j]);
   }
-  if constexpr (NC % 16 == 8) {
+  constexpr int c8 = NC / 16 * 16;
+  if constexpr (NC - c8 >= 8) {
     uint32_t r[8];
-    tc::ld_32x32b_x8(taddr + NC - 8, r);
+    tc::ld_32x32b_x8(taddr + c8, r);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[NC - 8 + j] = __uint_as_float(r[j]);
+    for (int j = 0; j < 8; ++j) v[c8 + j] = __uint_as_float(r[j]);
+  }
+  if constexpr (NC % 8 == 4) {
+    uint32_t r[4];
+    tc::ld_32x32b_x4(taddr + NC - 4, r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[NC - 4 + j] = __uint_as_float(r[j]);
+  }
+}
+
+// TMEM stores of NC (multiple of 4) consecutive columns from v.
+template <int NC>
+QWZ_DEVINL void st_cols(uint32_t taddr, const float (&v)[NC]) {
+#pragma unroll
+  for (int c = 0; c + 16 <= NC; c += 16) {
+    uint32_t r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(v[c + j]);
+    tc::st_32x32b_x16(taddr + c, r);
+  }
+  constexpr int c8 = NC / 16 * 16;
+  if constexpr (NC - c8 >= 8) {
+    uint32_t r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __float_as_uint(v[c8 + j]);
+    tc::st_32x32b_x8(taddr + c8, r);
+  }
+  if constexpr (NC % 8 == 4) {
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = __float_as_uint(v[NC - 4 + j]);
+    tc::st_32x32b_x4(taddr + NC - 4, r);
   }
 }
 
@@ -133,7 +188,7 @@ QWZ_DEVINL void ld_cols(uint32_t taddr, float (&v)[NC]) {
 // of two (FP16-exact), and the per-row score factor sm_scale*log2e/scale.
 template <typename T, int N>
 QWZ_DEVINL void stage_q(const SplitParams& p, int kvh, uint32_t qbase, float* rowfac, int mw, int lane) {
-  for (int r = mw; r < N; r += 8) {
+  for (int r = mw; r < N; r += kVtMathWarps) {
     const int qi = r / kGroup, hg = r - qi * kGroup;
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (qi < p.q_len) {
@@ -157,25 +212,34 @@ QWZ_DEVINL void stage_q(const SplitParams& p, int kvh, uint32_t qbase, float* ro
     }
     // d = 8 lane .. +7: k-atom lane / 8, 16-byte chunk lane % 8 of row r
     sts128(qbase + (lane >> 3) * (N * 128) + r * 128 + (((lane & 7) ^ (r & 7)) << 4), h[0], h[1], h[2], h[3]);
-    if (lane == 0) rowfac[r] = qi < p.q_len ? p.sm_scale_log2 / sc : 0.f;
+    // padding rows (zero Q) keep a positive factor so masked scores stay -inf
+    if (lane == 0) rowfac[r] = qi < p.q_len ? p.sm_scale_log2 / sc : p.sm_scale_log2;
   }
 }
 
-// Head-dim half h of token row tt of a K or V tile (the 64 code bytes of
-// chunks 4h..4h+3, 128-byte swizzle, and their 8 scales) as f16x2 words in
-// d order, handed to put(c, r16) per 32 values (code chunk c).  `zero`
-// (rows at or past the valid end) makes every value 0.
+// Head-dim part u (d in [D u, D u + D), D = 256 / kVtParts) of token row tt
+// of a K or V tile (code chunks kCh u .. kCh u + kCh - 1 of 32 values each,
+// 128-byte swizzle, and their 2 kCh scales) as f16x2 words in d order,
+// handed to put(g, r16) per code chunk g.  `zero` (rows at or past the valid
+// end) makes every value 0.
 template <class Put>
-QWZ_DEVINL void dequant_row_half(uint32_t codes, uint32_t scales, int tt, int h, bool zero, Put put) {
-  uint2 sc = lds64(scales + tt * kScaleBytes + 8 * h);
-  if (zero) sc = make_uint2(0u, 0u);
-  uint32_t s01, s23, s45, s67;
-  e4m3x4_to_f16x2x2(sc.x, s01, s23);
-  e4m3x4_to_f16x2x2(sc.y, s45, s67);
-  const uint32_t spair[4] = {s01, s23, s45, s67};
+QWZ_DEVINL void dequant_row_part(uint32_t codes, uint32_t scales, int tt, int u, bool zero, Put put) {
+  constexpr int kCh = 8 / kVtParts;
+  uint32_t spair[kCh];
+  if constexpr (kCh == 2) {
+    uint32_t sc = lds32(scales + tt * kScaleBytes + 4 * u);
+    if (zero) sc = 0u;
+    e4m3x4_to_f16x2x2(sc, spair[0], spair[1]);
+  } else {
+    uint2 sc = lds64(scales + tt * kScaleBytes + 8 * u);
+    if (zero) sc = make_uint2(0u, 0u);
+    e4m3x4_to_f16x2x2(sc.x, spair[0], spair[1]);
+    e4m3x4_to_f16x2x2(sc.y, spair[2], spair[3]);
+  }
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint4 w = lds128(codes + tt * kCodeBytes + (((4 * h + c) ^ (tt & 7)) << 4));
+  for (int c = 0; c < kCh; ++c) {
+    const int g = kCh * u + c;
+    const uint4 w = lds128(codes + tt * kCodeBytes + ((g ^ (tt & 7)) << 4));
     const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
     const uint32_t sA = __byte_perm(spair[c], 0, 0x1010), sB = __byte_perm(spair[c], 0, 0x3232);
     uint32_t r[16];
@@ -187,8 +251,34 @@ QWZ_DEVINL void dequant_row_half(uint32_t codes, uint32_t scales, int tt, int h,
 #pragma unroll
       for (int e = 0; e < 4; ++e) r[4 * j + e] = hmul2_u32(hv[e], sc2);
     }
-    put(c, r);
+    put(g, r);
   }
+}
+
+// Packed f32x2 arithmetic (one instruction for two lanes of work).
+QWZ_DEVINL void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+  uint64_t d;
+  asm("{\n .reg .b64 a, b, c;\n mov.b64 a, {%1, %2};\n mov.b64 b, {%3, %4};\n mov.b64 c, {%5, %6};\n"
+      " fma.rn.f32x2 %0, a, b, c;\n}\n"
+      : "=l"(d)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+QWZ_DEVINL void fadd2(float& a0, float& a1, float b0, float b1) {
+  uint64_t d;
+  asm("{\n .reg .b64 a, b;\n mov.b64 a, {%1, %2};\n mov.b64 b, {%3, %4};\n add.rn.f32x2 %0, a, b;\n}\n"
+      : "=l"(d)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(a0), "=f"(a1) : "l"(d));
+}
+QWZ_DEVINL float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+QWZ_DEVINL void sts64(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.u32 [%0], {%1,%2};\n" ::"r"(addr), "r"(a), "r"(b));
 }
 
 }  // namespace
@@ -197,7 +287,6 @@ template <typename T, int N>
 __global__ void __launch_bounds__(kVtWarps * 32, 1)
     nvfp4_verify_tc_kernel(const __grid_constant__ SplitParams p) {
   using L = VtLayout<N>;
-  constexpr int NH = N / 2;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sraw = smem_u32(smem);
   const uint32_t sb = (sraw + 1023u) & ~1023u;
@@ -226,15 +315,15 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
 #pragma unroll
     for (int s = 0; s < kVtKStages; ++s) {
       mbar_init(bar_kfull + 8 * s, 1);
-      mbar_init(bar_kempty + 8 * s, 8);
+      mbar_init(bar_kempty + 8 * s, kVtMathWarps);
     }
 #pragma unroll
     for (int s = 0; s < kVtVStages; ++s) {
       mbar_init(bar_vfull + 8 * s, 1);
-      mbar_init(bar_vempty + 8 * s, 8);
+      mbar_init(bar_vempty + 8 * s, kVtMathWarps);
     }
-    mbar_init(bar_kready, 8);
-    mbar_init(bar_pv, 8);
+    mbar_init(bar_kready, kVtMathWarps);
+    mbar_init(bar_pv, kVtMathWarps);
     mbar_init(bar_s, 1);
     mbar_init(bar_s + 8, 1);
     mbar_init(bar_o, 1);
@@ -303,14 +392,23 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     // ----------------------------------------------------------------- MMA
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t idesc_qk = tc::idesc_f16_f32(128, N);
-      constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, 2 * N, true, true);
+      constexpr uint32_t idesc_pv = tc::idesc_f16_f32(128, N, true, true);
+      // Descriptors are built once; a K step adds its byte offset / 16 to the
+      // start-address field (addresses stay below 256 KB, so no carry).  The
+      // issuing thread shares its scheduler with four math warps: every
+      // instruction it saves between two MMAs keeps the tensor pipe fed.
+      const uint64_t dq = tc::smem_desc_k128(sb + L::kQ);
+      const uint64_t dv = tc::smem_desc_mn128(sb + L::kVf, 16384, 1024);
+      const uint64_t dp = tc::smem_desc_mn128(sb + L::kP, 16384, 1024);
+      const uint32_t tk = tbase + kTmK, ts = tbase + kTmS, to = tbase + kTmO;
       auto qk = [&](int j) -> bool {
         if (!mbar_wait(bar_kready, j & 1)) return false;
         tc::fence_after();
+        const uint32_t d = ts + 64 * (j & 1);
 #pragma unroll
         for (int ks = 0; ks < 16; ++ks)
-          tc::mma_ts(tbase + kTmS + 64 * (j & 1), tbase + kTmK + 8 * ks,
-                     tc::smem_desc_k128(sb + L::kQ + (ks >> 2) * (N * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+          tc::mma_ts(d, tk + 8 * ks, dq + (uint64_t)(((ks >> 2) * (N * 128) + (ks & 3) * 32) >> 4), idesc_qk,
+                     ks > 0);
         tc::commit(bar_s + 8 * (j & 1));
         return true;
       };
@@ -324,9 +422,8 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            tc::mma_ss(tbase + kTmO + 2 * N * h,
-                       tc::smem_desc_mn128(sb + L::kVf + 2 * h * 16384 + ks * 2048, 16384, 1024),
-                       tc::smem_desc_mn128(sb + L::kP + ks * 2048, 16384, 1024), idesc_pv, (i > 0 || ks > 0));
+            tc::mma_ss(to + N * h, dv + (uint64_t)((2 * h * 16384 + ks * 2048) >> 4),
+                       dp + (uint64_t)((ks * 2048) >> 4), idesc_pv, (i > 0 || ks > 0));
         }
         tc::commit(bar_o);
       }
@@ -341,27 +438,36 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     }
   } else {
     // ---------------------------------------------------------------- math
-    const int q = warp & 3, h = (warp - kVtMath0) >> 2;
+    constexpr int NP = N / kVtParts;      // score columns of this warp
+    constexpr int NO = 2 * N / kVtParts;  // O^T columns this warp rescales and stores
+    static_assert(NP % 4 == 0, "P is stored in 8-byte pieces");
+    const int q = warp & 3, u = (warp - kVtMath0) >> 2;
+    const int ohalf = u & 1, ocol = (u >> 1) * NO;  // this warp's M half of O^T and first column
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int tt = 32 * q + lane;  // this thread's token row of K, V, S^T and P
-    float lsum[NH], mreg[NH];
+    const float* fac = rowfac + NP * u;
+    // nm = -(reference max); kMFloor stands for "no score yet": finite, so a
+    // masked score (-inf) stays -inf and a real one exceeds it by far more
+    // than kLazy
+    constexpr float kMFloor = -1e30f;
+    float lsum[NP], nm[NP];
 #pragma unroll
-    for (int c = 0; c < NH; ++c) {
+    for (int c = 0; c < NP; ++c) {
       lsum[c] = 0.f;
-      mreg[c] = -CUDART_INF_F;
+      nm[c] = -kMFloor;
     }
     bool ok = true;
 
-    // K(j) -> TMEM, thread = token tt, head-dim half h (columns 64h ..);
+    // K(j) -> TMEM, thread = token tt, head-dim part u (columns 16 g ..);
     // returns the tile's valid end, read before the ring slot is released
     auto do_k = [&](int j) -> int {
       const int s = j % kVtKStages;
       ok &= mbar_wait(bar_kfull + 8 * s, (j / kVtKStages) & 1);
       const int end = kstage_end[s];
       const uint32_t st = sb + L::kKRing + s * kVtHalfStage;
-      const uint32_t col = tbase + lane_base + kTmK + 64 * h;
-      dequant_row_half(st, st + kVtCodeBox, tt, h, false,
-                       [&](int c, const uint32_t (&r)[16]) { tc::st_32x32b_x16(col + 16 * c, r); });
+      const uint32_t col = tbase + lane_base + kTmK;
+      dequant_row_part(st, st + kVtCodeBox, tt, u, false,
+                       [&](int g, const uint32_t (&r)[16]) { tc::st_32x32b_x16(col + 16 * g, r); });
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_kempty + 8 * s);
       tc::wait_st();
@@ -380,33 +486,35 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       const int t0 = p.tok_begin + (rg.st_lo + (i >> 1)) * kPage + kVtTile * (i & 1);
       const int vend = vend_next;
 
-      float x[NH];
-      ld_cols<NH>(tbase + lane_base + kTmS + 64 * sbuf + NH * h, x);
+      float x[NP];
+      ld_cols<NP>(tbase + lane_base + kTmS + 64 * sbuf + NP * u, x);
       tc::wait_ld();
+      regs_ready(x);
       // S(i) is read and QK(i) is done: the K buffer takes K(i+1) now
       if (i + 1 < n_tiles) vend_next = do_k(i + 1);
 
       // ------------------------------------------------------- softmax(i)
-#pragma unroll
-      for (int c = 0; c < NH; c += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(rowfac + NH * h + c);
-        x[c] *= f.x;
-        x[c + 1] *= f.y;
-        x[c + 2] *= f.z;
-        x[c + 3] *= f.w;
-      }
       // causal / length mask only on tiles that reach the end
       if (t0 + kVtTile > min(vend, len_all - (p.q_len - 1))) {
         const int tok = t0 + tt;
 #pragma unroll
-        for (int c = 0; c < NH; ++c) {
-          const int qi = min((NH * h + c) / kGroup, p.q_len - 1);
+        for (int c = 0; c < NP; ++c) {
+          const int qi = min((NP * u + c) / kGroup, p.q_len - 1);
           if (tok >= min(vend, len_all - (p.q_len - 1 - qi))) x[c] = -CUDART_INF_F;
         }
       }
-      bool need = false;
+      // y = x * factor - max (base-2 units), two columns per instruction
+      float y[NP];
+      float ymax = -CUDART_INF_F;
 #pragma unroll
-      for (int c = 0; c < NH; ++c) need |= x[c] > mreg[c] + kLazy;
+      for (int c = 0; c < NP; c += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(fac + c);
+        ffma2(y[c], y[c + 1], x[c], x[c + 1], f.x, f.y, nm[c], nm[c + 1]);
+        ffma2(y[c + 2], y[c + 3], x[c + 2], x[c + 3], f.z, f.w, nm[c + 2], nm[c + 3]);
+        ymax = fmax3(ymax, y[c], y[c + 1]);
+        ymax = fmax3(ymax, y[c + 2], y[c + 3]);
+      }
+      const bool need = ymax > kLazy;
       const bool bad = !ok || *abort_flag;
       if (math_bar_or(need || bad)) {
         if (math_bar_or(bad)) {
@@ -416,50 +524,45 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
         }
         // move the reference max of every column to this tile's max
 #pragma unroll
-        for (int c = 0; c < NH; ++c) {
+        for (int c = 0; c < NP; ++c) {
           const float mx = warp_max(x[c]);
-          if (lane == 0) wred[(h * 4 + q) * NH + c] = mx;
+          if (lane == 0) wred[(u * 4 + q) * NP + c] = mx;
         }
         math_bar();
 #pragma unroll
-        for (int c = 0; c < NH; ++c) {
-          float tm = wred[(h * 4) * NH + c];
+        for (int c = 0; c < NP; ++c) {
+          float tm = wred[(u * 4) * NP + c];
 #pragma unroll
-          for (int qq = 1; qq < 4; ++qq) tm = fmaxf(tm, wred[(h * 4 + qq) * NH + c]);
-          const float mnew = fmaxf(mreg[c], tm);
-          const float alpha = mreg[c] == -CUDART_INF_F ? 0.f : exp2_approx(mreg[c] - mnew);
+          for (int qq = 1; qq < 4; ++qq) tm = fmaxf(tm, wred[(u * 4 + qq) * NP + c]);
+          const float mold = -nm[c];
+          const float mnew = fmaxf(mold, tm * fac[c]);  // factor > 0
+          const float alpha = exp2_approx(mold - mnew);  // 0 from kMFloor
           lsum[c] *= alpha;
-          mreg[c] = mnew;
-          if (q == 0 && lane == 0) alpha_s[NH * h + c] = alpha;
+          nm[c] = -mnew;
+          y[c] = fmaf(x[c], fac[c], -mnew);
+          if (q == 0 && lane == 0) alpha_s[NP * u + c] = alpha;
         }
         math_bar();
-        if (i > 0) {  // O^T of this quadrant and half, both P halves, after PV(i-1)
+        if (i > 0) {  // this warp's block of O^T (M half, column range), after PV(i-1)
           ok &= mbar_wait(bar_o, (i - 1) & 1);
           tc::fence_after();
+          const uint32_t oc = tbase + lane_base + kTmO + N * ohalf + ocol;
+          float ov[NO];
+          ld_cols<NO>(oc, ov);
+          tc::wait_ld();
+          regs_ready(ov);
 #pragma unroll
-          for (int c0 = 0; c0 < 2 * N; c0 += 16) {
-            uint32_t r[16];
-            tc::ld_32x32b_x16(tbase + lane_base + kTmO + 2 * N * h + c0, r);
-            tc::wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha_s[(c0 + j) % N]);
-            tc::st_32x32b_x16(tbase + lane_base + kTmO + 2 * N * h + c0, r);
-          }
+          for (int j = 0; j < NO; ++j) ov[j] *= alpha_s[ocol + j];
+          st_cols<NO>(oc, ov);
         }
         math_bar();  // alpha_s / wred are rewritten by the next slow tile
       }
-      uint32_t hw[NH / 2], lw[NH / 2];
+      uint32_t hw[NP / 2];
 #pragma unroll
-      for (int j = 0; j < NH / 2; ++j) {
-        const float m0 = mreg[2 * j] == -CUDART_INF_F ? 0.f : mreg[2 * j];
-        const float m1 = mreg[2 * j + 1] == -CUDART_INF_F ? 0.f : mreg[2 * j + 1];
-        const float p0 = exp2_approx(x[2 * j] - m0), p1 = exp2_approx(x[2 * j + 1] - m1);
-        lsum[2 * j] += p0;
-        lsum[2 * j + 1] += p1;
+      for (int j = 0; j < NP / 2; ++j) {
+        const float p0 = exp2_approx(y[2 * j]), p1 = exp2_approx(y[2 * j + 1]);
+        fadd2(lsum[2 * j], lsum[2 * j + 1], p0, p1);
         hw[j] = pack_half2(p0, p1);
-        const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[j]));
-        lw[j] = pack_half2(p0 - hf.x, p1 - hf.y);
       }
 
       // ------------------------------ V(i) and P(i) after PV(i-1) is done
@@ -468,26 +571,31 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
         const int s = i % kVtVStages;
         ok &= mbar_wait(bar_vfull + 8 * s, (i / kVtVStages) & 1);
         const uint32_t st = sb + L::kVRing + s * kVtHalfStage;
-        const uint32_t vrow = sb + L::kVf + 2 * h * 16384 + tt * 128;
-        dequant_row_half(st, st + kVtCodeBox, tt, h, t0 + tt >= vend, [&](int c, const uint32_t (&r)[16]) {
-          // d = 128h + 32c + 8j .. +7: atom 2h + c/2, 16-byte chunk 4(c%2) + j
+        const uint32_t vrow = sb + L::kVf + tt * 128;
+        dequant_row_part(st, st + kVtCodeBox, tt, u, t0 + tt >= vend, [&](int g, const uint32_t (&r)[16]) {
+          // d = 32g + 8j .. +7: atom g / 2 (64 d), 16-byte chunk 4 (g % 2) + j of the row
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            sts128(vrow + (c >> 1) * 16384 + (((4 * (c & 1) + j) ^ (tt & 7)) << 4), r[4 * j], r[4 * j + 1],
+            sts128(vrow + (g >> 1) * 16384 + (((4 * (g & 1) + j) ^ (tt & 7)) << 4), r[4 * j], r[4 * j + 1],
                    r[4 * j + 2], r[4 * j + 3]);
         });
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_vempty + 8 * s);
       }
       {
-        const uint32_t prow = sb + L::kP + tt * 128;
+        const uint32_t prow = sb + L::kP + tt * 128;  // N <= 64: one atom
+        if constexpr (NP % 8 == 0) {
 #pragma unroll
-        for (int c = 0; c < NH; c += 8) {
-          const int nh = NH * h + c, nl = N + NH * h + c;  // first column of the 16-byte chunk
-          sts128(prow + (nh >> 6) * 16384 + ((((nh & 63) >> 3) ^ (tt & 7)) << 4), hw[c / 2], hw[c / 2 + 1],
-                 hw[c / 2 + 2], hw[c / 2 + 3]);
-          sts128(prow + (nl >> 6) * 16384 + ((((nl & 63) >> 3) ^ (tt & 7)) << 4), lw[c / 2], lw[c / 2 + 1],
-                 lw[c / 2 + 2], lw[c / 2 + 3]);
+          for (int c = 0; c < NP; c += 8) {
+            const int n = NP * u + c;
+            sts128(prow + (((n >> 3) ^ (tt & 7)) << 4), hw[c / 2], hw[c / 2 + 1], hw[c / 2 + 2], hw[c / 2 + 3]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < NP; c += 4) {
+            const int n = NP * u + c;
+            sts64(prow + (((n >> 3) ^ (tt & 7)) << 4) + (n & 4) * 2, hw[c / 2], hw[c / 2 + 1]);
+          }
         }
       }
       fence_proxy_async_smem();  // V and P are read by the tensor core
@@ -503,39 +611,38 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
                         mbar_wait(bar_o, (n_tiles - 1) & 1);
     tc::fence_after();
 #pragma unroll
-    for (int c = 0; c < NH; ++c) {
+    for (int c = 0; c < NP; ++c) {
       const float lw = warp_sum(lsum[c]);
-      if (lane == 0) wred[(h * 4 + q) * NH + c] = lw;
-      if (q == 0 && lane == 0) mref_s[NH * h + c] = have_o ? mreg[c] : -CUDART_INF_F;
+      if (lane == 0) wred[(u * 4 + q) * NP + c] = lw;
+      if (q == 0 && lane == 0) mref_s[NP * u + c] = -nm[c];
     }
     math_bar();
     const int rows = kGroup * p.q_len;
-    if (q == 0 && lane < NH && NH * h + lane < rows) {
-      const int r = NH * h + lane;
+    if (q == 0 && lane < NP && NP * u + lane < rows) {
+      const int r = NP * u + lane;
       float l = 0.f;
 #pragma unroll
-      for (int qq = 0; qq < 4; ++qq) l += wred[(h * 4 + qq) * NH + lane];
+      for (int qq = 0; qq < 4; ++qq) l += wred[(u * 4 + qq) * NP + lane];
+      if (!have_o) l = 0.f;
       const size_t R = (size_t)(r / kGroup) * kQHeads + kvh * kGroup + r % kGroup;
       const size_t base = R * p.num_splits + split;
-      p.partial_ml[base * 2 + 0] = mref_s[r];
-      p.partial_ml[base * 2 + 1] = have_o ? l : 0.f;
+      p.partial_ml[base * 2 + 0] = l > 0.f ? mref_s[r] : -CUDART_INF_F;  // no key: empty split
+      p.partial_ml[base * 2 + 1] = l;
     }
-    const int d = 128 * h + tt;  // O^T lane tt of M half h
-#pragma unroll
-    for (int c0 = 0; c0 < N; c0 += 8) {
-      uint32_t hi[8], lo[8];
+    {
+      const int d = 128 * ohalf + tt;  // O^T lane tt of M half ohalf
+      float o[NO];
       if (have_o) {
-        tc::ld_32x32b_x8(tbase + lane_base + kTmO + 2 * N * h + c0, hi);
-        tc::ld_32x32b_x8(tbase + lane_base + kTmO + 2 * N * h + N + c0, lo);
+        ld_cols<NO>(tbase + lane_base + kTmO + N * ohalf + ocol, o);
         tc::wait_ld();
+        regs_ready(o);
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int r = c0 + j;
+      for (int j = 0; j < NO; ++j) {
+        const int r = ocol + j;
         if (r < rows) {
           const size_t R = (size_t)(r / kGroup) * kQHeads + kvh * kGroup + r % kGroup;
-          const float o = have_o ? __uint_as_float(hi[j]) + __uint_as_float(lo[j]) : 0.f;
-          p.partial_o[(R * p.num_splits + split) * kHeadDim + d] = o;
+          p.partial_o[(R * p.num_splits + split) * kHeadDim + d] = have_o ? o[j] : 0.f;
         }
       }
     }
