@@ -24,6 +24,11 @@
 //   PV  O^T[256 x 8] += V^T P^T, m-tile j row g <-> d = 32g + 2j (+1),
 //       P^T from movmatrix of the S^T fragment, split hi + lo in FP16.
 // Waits are bounded (kErrTimeout instead of a hang).
+//
+// The kernel is launched with programmatic stream serialisation: a CTA sets
+// up its shared memory and barriers while the previous kernel in the stream
+// drains, reads nothing from global memory before griddep_wait(), and lets
+// the combine launch begin once its page loop is done.
 
 #include "attn_common.cuh"
 #include "nvfp4_quant.cuh"
@@ -214,6 +219,22 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y;
 
+  // shared-memory set-up overlaps the previous kernel; global reads wait
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      meta->released[s] = 0;
+      meta->last_issued[s] = -1;
+    }
+    mbar_fence_init();
+    tma_prefetch_desc(&p.tm_kc);
+    tma_prefetch_desc(&p.tm_vc);
+    tma_prefetch_desc(&p.tm_ks);
+    tma_prefetch_desc(&p.tm_vs);
+  }
+  griddep_wait();
+
   // the table row is loaded while the length is in flight
   constexpr int kRowPerThread = kDecPidCache / (kDecWarps * 32);
   const int n_cached = min(p.table_width, kDecPidCache);
@@ -238,21 +259,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
   }
   const bool app_warp = k_app >= 0 && warp >= kDecWarps - 2;
   if (app_warp && k_app < kDecStages) fused_append<T>(p, app_pos, kvh, warp, lane);  // before the first issue
-  if (tid == 0) {
-#pragma unroll
-    for (int s = 0; s < kDecStages; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      meta->released[s] = 0;
-      meta->last_issued[s] = -1;
-    }
-    mbar_fence_init();
-  }
   __syncthreads();
   if (tid == 0 && rg.n_st > 0) {
-    tma_prefetch_desc(&p.tm_kc);
-    tma_prefetch_desc(&p.tm_vc);
-    tma_prefetch_desc(&p.tm_ks);
-    tma_prefetch_desc(&p.tm_vs);
     for (int k = 0; k < min(rg.n_st, kDecStages); ++k)
       issue_page(p, pid, meta, rg, k, k, sbase, bar_full, kvh);
   }
@@ -372,6 +380,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
     }
   }
   __syncthreads();
+  griddep_launch_dependents();
   decode_epilogue<kDecWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int d, int& gg, int& j) {
     gg = d >> 5;
     j = (d & 31) >> 1;
@@ -384,9 +393,7 @@ cudaError_t launch_nvfp4_decode(const SplitParams& p, cudaStream_t stream) {
   auto kernel = nvfp4_decode_kernel<T>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.num_splits, kKvHeads);
-  kernel<<<grid, kDecWarps * 32, kDecSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3(p.num_splits, kKvHeads), dim3(kDecWarps * 32), kDecSmemBytes, stream, p);
 }
 
 }  // namespace qwz

@@ -97,6 +97,8 @@ QWZ_DEVINL void issue_stage(const SplitParams& p, DrMeta* meta, const StageRange
 
 }  // namespace
 
+// Launched with programmatic stream serialisation: barriers are set up while
+// the previous kernel drains, global memory is read after griddep_wait().
 __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __grid_constant__ SplitParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sraw = smem_u32(smem);
@@ -107,8 +109,6 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y;
 
-  const StageRange rg = stage_range<kDrTokens>(p, split);
-
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kDrStages; ++s) {
@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
     }
     mbar_fence_init();
   }
+  griddep_wait();  // shared-memory set-up overlaps the previous kernel
+  const StageRange rg = stage_range<kDrTokens>(p, split);
   __syncthreads();
   if (tid == 0 && rg.n_st > 0) {
     tma_prefetch_desc(&p.tm_kc);
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
     }
   }
   __syncthreads();
+  griddep_launch_dependents();
   decode_epilogue<kDrWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int d, int& gg, int& j) {
     gg = (d & 127) >> 4;
     j = ((d >> 7) << 3) + ((d & 15) >> 1);
@@ -256,9 +259,7 @@ cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(fp8_draft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kDrSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.num_splits, kKvHeads);
-  fp8_draft_kernel<<<grid, kDrWarps * 32, kDrSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(fp8_draft_kernel, dim3(p.num_splits, kKvHeads), dim3(kDrWarps * 32), kDrSmemBytes, stream, p);
 }
 
 }  // namespace qwz

@@ -307,10 +307,6 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   float* wred = reinterpret_cast<float*>(sg + L::kWred);
   int* pid = reinterpret_cast<int*>(sg + L::kPid);
 
-  const StageRange rg = stage_range<kPage>(p, split);
-  const int n_tiles = 2 * rg.n_st;
-  const int len_all = __ldg(p.seqlens) + p.len_add;  // causal limits use the whole sequence
-
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kVtKStages; ++s) {
@@ -335,6 +331,12 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     tc::tmem_alloc(sb + L::kMeta + 16, kTmCols);
     tc::tmem_relinquish();
   }
+  // barriers and tensor memory are set up while the previous kernel drains;
+  // global memory (lengths, table, Q, pages) only after it completes
+  griddep_wait();
+  const StageRange rg = stage_range<kPage>(p, split);
+  const int n_tiles = 2 * rg.n_st;
+  const int len_all = __ldg(p.seqlens) + p.len_add;  // causal limits use the whole sequence
   if (warp == 0) {
     for (int i = lane; i < min(rg.n_st, kVtPidCache); i += 32)
       pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
@@ -648,6 +650,7 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     }
   }
 
+  griddep_launch_dependents();  // the combine may begin its launch
   tc::fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -664,9 +667,7 @@ cudaError_t launch_verify_tc_n(const SplitParams& p, cudaStream_t stream) {
   auto kernel = nvfp4_verify_tc_kernel<T, N>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.num_splits, kKvHeads);
-  kernel<<<grid, kVtWarps * 32, L::kBytes, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kernel, dim3(p.num_splits, kKvHeads), dim3(kVtWarps * 32), L::kBytes, stream, p);
 }
 
 template <typename T>

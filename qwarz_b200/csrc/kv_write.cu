@@ -27,6 +27,8 @@ template <typename T>
 __global__ void __launch_bounds__(64) nvfp4_append_kernel(const AppendParams p) {
   const int i = blockIdx.x, h = blockIdx.y;
   const int tensor = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_wait();               // the new rows come from the previous kernel
+  griddep_launch_dependents();  // the attention kernel may begin its launch
   const int pos = __ldg(p.seqlens) + i;
   const int lp = (pos >> 8) - p.table_page_offset;
   if (pos < 0 || lp < 0 || lp >= p.table_width) {
@@ -117,12 +119,9 @@ __global__ void __launch_bounds__(128) nvfp4_gather_kernel(const GatherParams p)
 
 cudaError_t launch_nvfp4_append(const AppendParams& p, int dtype, cudaStream_t stream) {
   if (p.append_len <= 0) return cudaSuccess;
-  dim3 grid(p.append_len, p.num_kv_heads);
-  if (dtype == kDtypeBF16)
-    nvfp4_append_kernel<__nv_bfloat16><<<grid, 64, 0, stream>>>(p);
-  else
-    nvfp4_append_kernel<__half><<<grid, 64, 0, stream>>>(p);
-  return cudaGetLastError();
+  const dim3 grid(p.append_len, p.num_kv_heads);
+  if (dtype == kDtypeBF16) return launch_pdl(nvfp4_append_kernel<__nv_bfloat16>, grid, dim3(64), 0, stream, p);
+  return launch_pdl(nvfp4_append_kernel<__half>, grid, dim3(64), 0, stream, p);
 }
 
 cudaError_t launch_fp8_write(const Fp8WriteParams& p, int dtype, cudaStream_t stream) {

@@ -220,6 +220,35 @@ QWZ_DEVINL void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// A kernel launched with the programmatic-stream-serialization attribute may
+// start while its predecessor in the stream is still running: it must not
+// read memory the predecessor writes (or write memory it reads) before
+// griddep_wait(), which returns once the predecessor grid has completed and
+// its writes are visible.  Without the attribute both are no-ops.
+// griddep_launch_dependents() lets the next kernel in the stream begin its
+// launch (its own griddep_wait() still waits for this grid to finish).
+QWZ_DEVINL void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+QWZ_DEVINL void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+// Host: launch with programmatic stream serialisation (the kernel calls
+// griddep_wait() before touching memory its predecessor may write).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // 128-byte-row XOR swizzle of 16-byte chunks (rows of 128 B, chunk 0..7);
 // the layout a TMA tiled load with CU_TENSOR_MAP_SWIZZLE_128B produces in a
 // 1024-byte aligned destination.
