@@ -1,6 +1,6 @@
 // Device helpers shared by the split-K attention kernels (decode, verify,
 // FP8 draft): Q fragment loading, stage partitioning, page lookup, the
-// base-2 online softmax with lazy rescaling, the hi/lo FP16 split of P and
+// base-2 online softmax with lazy rescaling, the FP16 P fragments and
 // the cross-warp (m, l, O) merge of the decode layout.
 #pragma once
 
@@ -123,22 +123,17 @@ QWZ_DEVINL int lookup_page(const SplitParams& p, int t, bool report) {
   return pp;
 }
 
-// P (FP32) as two FP16 B-fragments hi + lo with hi + lo = P to ~2^-22
-// relative, so the PV product through FP16 tensor cores keeps FP32-level
-// accuracy (one extra MMA per tile, no extra dequantisation).
+// P (FP32) as the FP16 B-fragments of the PV product: P is rounded to FP16
+// once, the precision of the PV operand in the reference's XQA kernel
+// (the S^T c-fragment is transposed into the P^T b-fragment by movmatrix).
 struct PFrag {
-  uint32_t hi0, hi1, lo0, lo1;
+  uint32_t hi0, hi1;
 };
 
 QWZ_DEVINL PFrag p_fragments(float p0, float p1, float p2, float p3) {
   PFrag f;
-  const uint32_t h01 = pack_half2(p0, p1), h23 = pack_half2(p2, p3);
-  const float2 r01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-  const float2 r23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  f.hi0 = movmatrix_trans(h01);
-  f.hi1 = movmatrix_trans(h23);
-  f.lo0 = movmatrix_trans(pack_half2(p0 - r01.x, p1 - r01.y));
-  f.lo1 = movmatrix_trans(pack_half2(p2 - r23.x, p3 - r23.y));
+  f.hi0 = movmatrix_trans(pack_half2(p0, p1));
+  f.hi1 = movmatrix_trans(pack_half2(p2, p3));
   return f;
 }
 

@@ -22,7 +22,9 @@
 //       heads (padded to 8) on N, lane quad q's k-step s covering
 //       d = 64q + 4s + {0..3} so each A register is one code byte;
 //   PV  O^T[256 x 8] += V^T P^T, m-tile j row g <-> d = 32g + 2j (+1),
-//       P^T from movmatrix of the S^T fragment, split hi + lo in FP16.
+//       P^T from movmatrix of the S^T fragment, P in FP16 (the PV operand
+//       precision of the reference's XQA kernel; measured on B200 the hi + lo
+//       split it replaced cost 10 % at 262K for one extra MMA per tile).
 // Waits are bounded (kErrTimeout instead of a hang).
 //
 // The kernel is launched with programmatic stream serialisation: a CTA sets
@@ -118,7 +120,7 @@ QWZ_DEVINL void v_tile_load(uint32_t codes, uint32_t scales, int ra, int g, bool
   e4m3x4_to_f16x2x2(__byte_perm(sc16, sd16, 0x5140), v.scd0, v.scd1);
 }
 
-// O^T[m-tiles 4*w4 .. 4*w4+3] += V^T P^T for one tile (hi and lo halves of P).
+// O^T[m-tiles 4*w4 .. 4*w4+3] += V^T P^T for one tile.
 QWZ_DEVINL void pv_tile_word(const VTile& v, int w4, const PFrag& pf, float (&o)[16][4]) {
   const uint32_t xab = (v.a[w4] & 0x0F0F0F0Fu) | ((v.b[w4] << 4) & 0xF0F0F0F0u);
   const uint32_t yab = ((v.a[w4] >> 4) & 0x0F0F0F0Fu) | (v.b[w4] & 0xF0F0F0F0u);
@@ -136,7 +138,6 @@ QWZ_DEVINL void pv_tile_word(const VTile& v, int w4, const PFrag& pf, float (&o)
     const uint32_t a0 = hmul2_u32(hxab[kk], sab), a1 = hmul2_u32(hyab[kk], sab);
     const uint32_t a2 = hmul2_u32(hxcd[kk], scd), a3 = hmul2_u32(hycd[kk], scd);
     mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.hi0, pf.hi1);
-    mma_16816(o[4 * w4 + kk], a0, a1, a2, a3, pf.lo0, pf.lo1);
   }
 }
 

@@ -18,7 +18,8 @@
 //       {0..3}; each A register is a byte pair through cvt.rn.f16x2.e4m3x2.
 //   PV: lane row g covers chunk g of both halves (d = 16g + {0..15} and
 //       128 + 16g + {0..15}); tokens are paired with prmt before the convert.
-// The K scale multiplies S, the V scale multiplies P (split hi + lo).
+// The K scale multiplies S, the V scale multiplies P (FP16, as the
+// reference's Triton draft kernel feeds its PV dot).
 
 #include "attn_common.cuh"
 
@@ -216,7 +217,6 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
           e4m3x4_to_f16x2x2(__byte_perm(VA[w], VB[w], sel), a0, a1);
           e4m3x4_to_f16x2x2(__byte_perm(VC[w], VD[w], sel), a2, a3);
           mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.hi0, pf.hi1);
-          mma_16816(o[8 * half + 2 * w + pr], a0, a1, a2, a3, pf.lo0, pf.lo1);
         }
       }
     }

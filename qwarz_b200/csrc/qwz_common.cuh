@@ -146,6 +146,9 @@ QWZ_DEVINL uint32_t lds8(uint32_t addr) {
   asm volatile("ld.shared.u8 %0, [%1];\n" : "=h"(v) : "r"(addr));
   return v;
 }
+QWZ_DEVINL void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d));
+}
 QWZ_DEVINL void sts32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(v));
 }
