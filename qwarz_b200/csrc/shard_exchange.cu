@@ -84,31 +84,70 @@ __global__ void __launch_bounds__(256) shard_exchange_kernel(const ExchangeParam
   const int tid = threadIdx.x, grp = tid >> 5, lane = tid & 31;
   const int S = p.num_splits, rows = p.rows;
 
+  griddep_wait();               // the split partials come from the previous kernel
+  griddep_launch_dependents();  // the next kernel may begin its launch
   // ---------------------------------------------- 1. this rank's record
   const float* ml = p.pml[y] + (size_t)r * S * 2;
   const float* po = p.po[y] + (size_t)r * S * kHeadDim + lane * 8;
-  float M = -CUDART_INF_F;
-  for (int s = tid; s < S; s += 256) M = fmaxf(M, ml[2 * s]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if (lane == 0) red_m[grp] = M;
   if (tid == 0) s_epoch = p.epochs[y][r] + 1u;
-  __syncthreads();
-  M = red_m[0];
-#pragma unroll
-  for (int i = 1; i < GROUPS; ++i) M = fmaxf(M, red_m[i]);
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float ls = 0.f;
-  if (M != -CUDART_INF_F) {
+  float ls = 0.f, M = -CUDART_INF_F;
+  constexpr int J = 8;  // splits per group held in registers (64 per row in one batch)
+  if (S <= GROUPS * J) {
+    // one batch of loads: the group's (m, l) and O slices, then the row max
+    float mv[J], lv[J];
+    float4 oa[J], ob[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int s = grp + GROUPS * j;
+      mv[j] = -CUDART_INF_F;
+      lv[j] = 0.f;
+      oa[j] = ob[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s < S) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(ml) + s);
+        mv[j] = v.x;
+        lv[j] = v.y;
+        oa[j] = __ldcg(reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim));
+        ob[j] = __ldcg(reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim + 4));
+      }
+    }
+    float mloc = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < J; ++j) mloc = fmaxf(mloc, mv[j]);
+    if (lane == 0) red_m[grp] = mloc;
+    __syncthreads();
+    M = red_m[0];
+#pragma unroll
+    for (int i = 1; i < GROUPS; ++i) M = fmaxf(M, red_m[i]);
+    if (M != -CUDART_INF_F) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) {  // empty splits (m = -inf, O = 0) weigh 0
+        const float w = mv[j] == -CUDART_INF_F ? 0.f : exp2_approx(mv[j] - M);
+        ls += w * lv[j];
+        acc[0] += w * oa[j].x; acc[1] += w * oa[j].y; acc[2] += w * oa[j].z; acc[3] += w * oa[j].w;
+        acc[4] += w * ob[j].x; acc[5] += w * ob[j].y; acc[6] += w * ob[j].z; acc[7] += w * ob[j].w;
+      }
+    }
+  } else {
+    for (int s = tid; s < S; s += 256) M = fmaxf(M, ml[2 * s]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    if (lane == 0) red_m[grp] = M;
+    __syncthreads();
+    M = red_m[0];
+#pragma unroll
+    for (int i = 1; i < GROUPS; ++i) M = fmaxf(M, red_m[i]);
+    if (M != -CUDART_INF_F) {
 #pragma unroll 4
-    for (int s = grp; s < S; s += GROUPS) {  // empty splits (m = -inf, O = 0) weigh 0
-      const float m = ml[2 * s];
-      const float w = m == -CUDART_INF_F ? 0.f : exp2_approx(m - M);
-      ls += w * ml[2 * s + 1];
-      const float4 a = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim);
-      const float4 b = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim + 4);
-      acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
-      acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
+      for (int s = grp; s < S; s += GROUPS) {  // empty splits (m = -inf, O = 0) weigh 0
+        const float m = ml[2 * s];
+        const float w = m == -CUDART_INF_F ? 0.f : exp2_approx(m - M);
+        ls += w * ml[2 * s + 1];
+        const float4 a = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim);
+        const float4 b = *reinterpret_cast<const float4*>(po + (size_t)s * kHeadDim + 4);
+        acc[0] += w * a.x; acc[1] += w * a.y; acc[2] += w * a.z; acc[3] += w * a.w;
+        acc[4] += w * b.x; acc[5] += w * b.y; acc[6] += w * b.z; acc[7] += w * b.w;
+      }
     }
   }
 #pragma unroll
@@ -178,7 +217,10 @@ cudaError_t launch_shard_exchange(const ExchangeParams& p, int emulated, int dty
                                     : (const void*)shard_exchange_kernel<__half>;
   if (emulated)  // ranks that wait on one another must be co-resident
     return cudaLaunchCooperativeKernel(kernel, grid, dim3(256), args, 0, stream);
-  return cudaLaunchKernel(kernel, grid, dim3(256), args, 0, stream);
+  // one real rank: launched with programmatic stream serialisation (the
+  // kernel reads the split partials only after griddep_wait())
+  if (dtype == kDtypeBF16) return launch_pdl(shard_exchange_kernel<__nv_bfloat16>, grid, dim3(256), 0, stream, p);
+  return launch_pdl(shard_exchange_kernel<__half>, grid, dim3(256), 0, stream, p);
 }
 
 }  // namespace qwz
