@@ -306,6 +306,13 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
       if (tw + g + 24 >= valid_end) t[6] = t[7] = -CUDART_INF_F;
     }
 
+    // V fragments first: their shared-memory latency hides behind the softmax
+    const uint32_t vcodes = st + kDecCodeTile;
+    const uint32_t vscales = st + 2 * kDecCodeTile + kDecScaleTile;
+    VTile va, vb;
+    v_tile_load(vcodes, vscales, vA, g, tail, t0 + vA, valid_end, va);
+    v_tile_load(vcodes, vscales, vA + 16, g, tail, t0 + vA + 16, valid_end, vb);
+
     // ---------------- one online-softmax update for the 32 tokens
     float mx0 = fmaxf(fmaxf(t[0], t[2]), fmaxf(t[4], t[6]));
     float mx1 = fmaxf(fmaxf(t[1], t[3]), fmaxf(t[5], t[7]));
@@ -343,11 +350,6 @@ __global__ void __launch_bounds__(kDecWarps * 32, 1)
     const PFrag pB = p_fragments(t[4], t[5], t[6], t[7]);
 
     // ---------------- O^T += V^T P^T for both tiles
-    const uint32_t vcodes = st + kDecCodeTile;
-    const uint32_t vscales = st + 2 * kDecCodeTile + kDecScaleTile;
-    VTile va, vb;
-    v_tile_load(vcodes, vscales, vA, g, tail, t0 + vA, valid_end, va);
-    v_tile_load(vcodes, vscales, vA + 16, g, tail, t0 + vA + 16, valid_end, vb);
 #pragma unroll
     for (int w4 = 0; w4 < 4; ++w4) {
       pv_tile_word(va, w4, pA, o);
