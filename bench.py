@@ -465,6 +465,40 @@ def run_extra(args, device) -> dict:
             v7["tensor_TFLOPs_split"] = v7["verify_flops_per_layer"] / (v7["split_us_per_launch"] * 1e-6) / 1e12
             res["configs"][f"c3_{tokens}"] = {"verify_q7": v7, "decode_q1": d1,
                                               "verify_over_decode_step": v7["us_per_step"] / d1["us_per_step"]}
+    if args.workload in ("prefill", "all"):
+        # NVFP4 prefill (SURVEY next item 1): one launch over the pages vs the
+        # 8-row-window route through the verify kernel it replaces
+        for pre, S in ((0, 8192), (61440, 4096)):
+            tokens = pre + S
+            pages = (tokens + PAGE - 1) // PAGE
+            c, perm = build_layer(ops, device, pages, tokens, seed=5000 + S)
+            q = torch.randn(S, HEADS, DIM, generator=g, device=device).to(dtype)
+            out = torch.empty_like(q)
+            pre_t = torch.tensor([pre], dtype=torch.int32, device=device)
+
+            def prefill():
+                ops.nvfp4_prefill(q, c[0], c[1], c[2], c[3], perm, pre_t, out)
+
+            splits = ops.default_splits(device, tokens, 8)
+            po, pml = ops.split_workspace(device, 8, splits)
+            wl = torch.arange(pre, pre + S, 8, dtype=torch.int32, device=device)
+
+            def windows():
+                for w in range(S // 8):
+                    ops.attn_split(q[8 * w:8 * w + 8], c[0], c[1], perm, wl[w:w + 1], po, pml, c[2], c[3], splits)
+                    ops.attn_combine(po, pml, out[8 * w:8 * w + 8], splits)
+
+            for _ in range(2):
+                prefill()
+            ms = cuda_time(prefill, 5, stream) / 5
+            ms_w = graph_time_ms(windows, 1, 2, stream)  # the old route, graph-captured
+            flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
+            res["configs"][f"prefill_{pre}+{S}"] = {
+                "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+                "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
+                "windowed_verify_us": ms_w * 1e3, "speedup_vs_windows": ms_w / ms}
+            del c, perm
+            torch.cuda.empty_cache()
     if args.workload in ("c4", "all"):
         res["configs"]["c4_262144_1gpu"] = nvfp4_config(262144, 1, 16)
     if args.workload in ("c5", "all"):
@@ -614,8 +648,8 @@ def main():
                          "rank can reach every GPU, else NCCL)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c3", "c4", "c5", "all", "profile_decode", "profile_verify",
-                             "profile_draft"],
+                    choices=["auto", "c3", "c4", "c5", "prefill", "all", "profile_decode",
+                             "profile_verify", "profile_draft"],
                     help="auto: the driver's headline (C2 at N=1, weak-scaled sharding at N>1); "
                          "c3/c4/c5/all: the other BASELINE configs on one GPU (separate JSON); "
                          "profile_*: three eager launches of one kernel on one 65,536-token layer, "

@@ -131,6 +131,21 @@ int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache,
                      int32_t num_splits, float sm_scale, int32_t dtype, void* stream);
 
 /*
+ * NVFP4 paged prefill attention: q [q_len, 24, 256] (FP16/BF16) over the
+ * cache that already holds the q_len new rows (qwz_nvfp4_append first);
+ * query position s sees keys j <= cache_seqlens[0] + s (lower-right causal),
+ * out [q_len, 24, 256] same type.  Replaces the reference's staged prefill
+ * route (src/qwasar_runtime/xqa.py:612-768: gather NVFP4 -> FP16 scratch ->
+ * FP8 repage -> PRIMS / SDPA) with one launch that reads the NVFP4 pages
+ * directly; the semantics are those of `_flash_prefill` (xqa.py:612-673).
+ * No workspace.  Grid = ceil(q_len / 21) x 4 KV heads.
+ */
+int qwz_nvfp4_prefill(const void* q, const void* k_cache, const void* v_cache, const void* k_scales,
+                      const void* v_scales, const int32_t* block_table, const int32_t* cache_seqlens,
+                      void* out, int32_t table_width, int32_t num_pages, int32_t q_len, float sm_scale,
+                      int32_t dtype, void* stream);
+
+/*
  * qwz_nvfp4_attend without a caller-supplied workspace.  No counterpart in
  * the reference: it exists for callers that cannot allocate device memory
  * (an engine that owns every allocation, a fixed memory pool, an FFI that

@@ -11,13 +11,11 @@ Mirrors the reference operator the engine calls:
     (xqa.py:909-920).
 The decode/verify route (q_len <= 8) is one append + one split-K launch +
 one combine of the sm_100a kernels in libqwz_b200.so; there is no CPU
-fallback.  q_len > 8 (prefill) runs the verify kernel over windows of 8
-query rows after one append — correct, not yet a dedicated prefill kernel.
+fallback.  q_len > 8 (prefill) runs the NVFP4 prefill kernel after one append.
 """
 from __future__ import annotations
 
 import dataclasses
-import math
 import weakref
 from collections import Counter
 from contextlib import contextmanager
@@ -82,7 +80,6 @@ class _LayerState:
     workspaces: dict = field(default_factory=dict)
     graphs: dict = field(default_factory=dict)
     graph_calls: Counter = field(default_factory=Counter)
-    prefill_lens: torch.Tensor | None = None
 
 
 @dataclass
@@ -224,28 +221,15 @@ class NVFP4AttentionAdapter:
         return out
 
     def _prefill(self, args, state: _LayerState) -> torch.Tensor:
-        """q_len > 8: one append, then the verify kernel over windows of 8
-        query rows, window c seeing tokens <= pre + c*8 + r (lower-right
-        causal, as xqa.py:662)."""
+        """q_len > 8: one append, then one NVFP4 prefill launch over the
+        pages (query position s sees keys j <= pre + s, lower-right causal as
+        xqa.py:662); replaces the reference's gather -> FP16 -> FP8 -> PRIMS /
+        SDPA staging (xqa.py:612-768)."""
         ops.nvfp4_append(args.k, args.v, args.k_cache, args.v_cache, args.k_scales,
                          args.v_scales, args.block_table, args.cache_seqlens)
         out = torch.empty_like(args.q) if not _capturing() else self._output(state, args)
-        windows = math.ceil(args.q_len / XQA_MAX_QUERY)
-        if state.prefill_lens is None or state.prefill_lens.numel() < windows:
-            state.prefill_lens = torch.empty(max(windows, 16), dtype=torch.int32, device=args.q.device)
-        offsets = torch.arange(0, windows * XQA_MAX_QUERY, XQA_MAX_QUERY, dtype=torch.int32,
-                               device=args.q.device)
-        torch.add(offsets, args.cache_seqlens.view(-1)[:1], out=state.prefill_lens[:windows])
-        q_rows = args.q.view(args.q_len, HEADS, HEAD_DIM)
-        o_rows = out.view(args.q_len, HEADS, HEAD_DIM)
-        for w in range(windows):
-            r0 = w * XQA_MAX_QUERY
-            n = min(XQA_MAX_QUERY, args.q_len - r0)
-            splits, po, pml = self._workspace(state, args, n)
-            lens = state.prefill_lens[w:w + 1]
-            ops.attn_split(q_rows[r0:r0 + n], args.k_cache, args.v_cache, args.block_table, lens,
-                           po, pml, args.k_scales, args.v_scales, splits, 0, float(args.sm_scale))
-            ops.attn_combine(po, pml, o_rows[r0:r0 + n], splits)
+        ops.nvfp4_prefill(args.q, args.k_cache, args.v_cache, args.k_scales, args.v_scales,
+                          args.block_table, args.cache_seqlens, out, float(args.sm_scale))
         return out
 
     def _capture(self, state: _LayerState, args) -> _Graph:
@@ -287,8 +271,8 @@ class NVFP4AttentionAdapter:
         if args.q_len > XQA_MAX_QUERY:
             out = self._prefill(args, state)
             self.append_calls += 1
-            self.routes["prefill_windows"] += 1
-            self.query_rows["prefill_windows"] += args.q_len
+            self.routes["prefill"] += 1
+            self.query_rows["prefill"] += args.q_len
             return out
         if self.decode_graphs and not _capturing():
             key = (args.q_len, float(args.sm_scale), args.q.dtype)
@@ -343,7 +327,7 @@ class NVFP4AttentionAdapter:
                 "kernel_lengths": "post-append = pre-append + actual K rows (on device)",
                 "append_owner": "selected adapter route exactly once",
                 "short_query": "Q1..8",
-                "prefill": "Q>8 verify kernel over 8-row windows after one append",
+                "prefill": "Q>8: one append, then the NVFP4 prefill kernel (tcgen05) over the pages",
             },
             "routes": dict(self.routes),
             "query_rows": dict(self.query_rows),

@@ -320,6 +320,38 @@ int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache,
                   "qwz_nvfp4_attend(combine)");
 }
 
+int qwz_nvfp4_prefill(const void* q, const void* k_cache, const void* v_cache, const void* k_scales,
+                      const void* v_scales, const int32_t* block_table, const int32_t* cache_seqlens,
+                      void* out, int32_t table_width, int32_t num_pages, int32_t q_len, float sm_scale,
+                      int32_t dtype, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (!q || !aligned(q, 16) || !out || !aligned(out, 16))
+    return fail(QWZ_EINVAL, "q and out must be non-null 16-byte aligned pointers");
+  rc = check_nvfp4_cache(k_cache, v_cache, k_scales, v_scales, num_pages);
+  if (rc) return rc;
+  if (!block_table || !cache_seqlens) return fail(QWZ_EINVAL, "block_table and cache_seqlens are required");
+  if (table_width <= 0) return fail(QWZ_EINVAL, "table_width must be positive");
+  if (q_len < 1) return fail(QWZ_EINVAL, "q_len must be positive");
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return fail(QWZ_EINVAL, "sm_scale must be positive and finite");
+  qwz::PrefillParams p{};
+  p.q = q;
+  p.out = out;
+  p.block_table = block_table;
+  p.seqlens = cache_seqlens;
+  p.table_width = table_width;
+  p.num_pages = num_pages;
+  p.q_len = q_len;
+  p.sm_scale_log2 = sm_scale * kLog2e;
+  const uint64_t rows = (uint64_t)num_pages * qwz::kPage;
+  rc = encode_2d(&p.tm_kc, k_cache, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64u, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_2d(&p.tm_vc, v_cache, qwz::kRowBytesCodes, rows, qwz::kCodeBytes, 64u, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_2d(&p.tm_ks, k_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64u, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!rc) rc = encode_2d(&p.tm_vs, v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64u, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  return launched(qwz::launch_nvfp4_prefill(p, dtype, as_stream(stream)), "qwz_nvfp4_prefill");
+}
+
 int qwz_attn_shard_partial(const void* q, const void* k_cache, const void* v_cache,
                            const void* k_scales, const void* v_scales, const int32_t* block_table,
                            const int32_t* cache_seqlens, float* partial_o, float* partial_ml,

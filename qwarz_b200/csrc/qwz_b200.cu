@@ -2,6 +2,7 @@
 // error word (qwz::g_qwz_device_error) without relocatable device code.
 #include "attn_decode.cu"
 #include "attn_verify_tc.cu"
+#include "attn_prefill.cu"
 #include "attn_split.cu"
 #include "attn_draft.cu"
 #include "attn_combine.cu"

@@ -47,6 +47,21 @@ struct alignas(64) SplitParams {
   const void* app_v;
 };
 
+// NVFP4 paged prefill attention (attn_prefill.cu): q [q_len, 24, 256] over
+// the post-append cache, lower-right causal.  Tensor maps as SplitParams
+// but with 64-row boxes.
+struct alignas(64) PrefillParams {
+  CUtensorMap tm_kc, tm_vc, tm_ks, tm_vs;
+  const void* q;                 // [q_len, 24, 256] FP16/BF16
+  void* out;                     // [q_len, 24, 256] same type
+  const int32_t* block_table;
+  const int32_t* seqlens;        // pre-append length [1]
+  int table_width;
+  int num_pages;
+  int q_len;
+  float sm_scale_log2;
+};
+
 // LSE combine of split partials.  Row r, split s reads
 //   m,l at pml[r*ml_row + s*ml_split + {0,1}] and O at po[r*o_row + s*o_split + d].
 struct CombineParams {
@@ -115,6 +130,7 @@ struct ExchangeParams {
 };
 
 cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_nvfp4_prefill(const PrefillParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_shard_exchange(const ExchangeParams& p, int emulated, int dtype, cudaStream_t stream);
 cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStream_t stream);

@@ -215,6 +215,26 @@ def nvfp4_attend(q, k, v, k_cache, v_cache, k_scales, v_scales, block_table, cac
         _stream(dev)), "qwz_nvfp4_attend")
 
 
+def nvfp4_prefill(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens, out,
+                  sm_scale: float = DIM ** -0.5) -> None:
+    """Prefill attention of q [.., S, 24, 256] over the cache that already
+    holds the S new rows (nvfp4_append first): query position s sees keys
+    j <= cache_seqlens[0] + s.  Writes out (same shape and type as q)."""
+    dev = _cuda(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens, out)
+    P = check_cache(k_cache, v_cache, k_scales, v_scales)
+    _check_lengths(block_table, cache_seqlens)
+    _contig("q", q)
+    _contig("out", out)
+    if out.dtype != q.dtype or out.numel() != q.numel():
+        raise ValueError("out must match q")
+    S = q.numel() // (HEADS * DIM)
+    lib = _lib.load()
+    _lib.check(lib.qwz_nvfp4_prefill(
+        _p(q), _p(k_cache), _p(v_cache), _p(k_scales), _p(v_scales), _p(block_table),
+        _p(cache_seqlens), _p(out), block_table.shape[-1], P, S, float(sm_scale),
+        _dtype_code(q.dtype), _stream(dev)), "qwz_nvfp4_prefill")
+
+
 def shard_partial(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
                   partial_o, partial_ml, send_buf, tok_begin: int, tok_span: int,
                   num_splits: int, sm_scale: float = DIM ** -0.5) -> None:
