@@ -19,11 +19,13 @@
 //   warp 4      TMA producer: K and V codes + scales of a tile (2 x 9 KB)
 //               into 3-deep rings;
 //   warp 5      TMEM owner (512 columns) and MMA issuer (one thread);
-//   warps 6-13  dequant: K and V of a tile -> FP16 [64 tok][256 d] in
-//               shared memory (4 head-dim atoms of 64 tok x 128 B, 128-byte
-//               swizzle), thread = (token, quarter of d).  The same bytes
-//               are the K-major B operand of QK and the MN-major B operand
-//               of PV.
+//   warps 6-9   dequant K, warps 10-13 dequant V: a tile -> FP16
+//               [64 tok][256 d] in shared memory (4 head-dim atoms of 64 tok
+//               x 128 B, 128-byte swizzle), thread = (token, half of d).  The
+//               same bytes are the K-major B operand of QK and the MN-major
+//               B operand of PV.  K has two buffers, so K(j+1) is written
+//               while QK(j) reads K(j); V has one, written once PV(j-1) is
+//               done.
 // Per tile j:
 //   QK(j)  S[128 rows x 64 tok] = Q K^T, A = Q (K-major in shared memory,
 //          rows scaled by a power of two so they convert to FP16 exactly),
@@ -31,8 +33,7 @@
 //   soft   base-2 online softmax per row; P in FP16 (the reference's PV
 //          operand precision) written to TMEM as the A operand of PV;
 //   PV(j)  O[128 x 256] += P V(j), A = P from TMEM, B = V(j) MN-major.
-// The MMA thread issues QK(j+1) ahead of PV(j).  K(j+1) is dequantised as
-// soon as QK(j) has read K(j), V(j+1) once PV(j) has read V(j).  Every wait
+// The MMA thread issues QK(j+1) ahead of PV(j).  Every wait
 // is bounded; a role that times out raises the abort flag and the others
 // leave at their next wait.
 
@@ -50,23 +51,24 @@ constexpr int kPfStages = 3;                           // TMA ring depth (tiles)
 constexpr int kPfSoftWarps = 4;                        // warps 0-3
 constexpr int kPfProd = 4;                             // TMA producer warp
 constexpr int kPfMma = 5;                              // TMEM owner + MMA issuer
-constexpr int kPfDq0 = 6;                              // first dequant warp
-constexpr int kPfDqWarps = 8;
-constexpr int kPfWarps = kPfDq0 + kPfDqWarps;          // 14
-constexpr int kPfPidCache = 1024;                      // table entries staged in smem
+constexpr int kPfDq0 = 6;                              // first dequant warp (K: 6-9, V: 10-13)
+constexpr int kPfDqWarps = 4;                          // per tensor
+constexpr int kPfWarps = kPfDq0 + 2 * kPfDqWarps;      // 14
+constexpr int kPfPidCache = 512;                       // table entries staged in smem
+constexpr int kPfTileBytes = 4 * kPfTok * 128;         // one FP16 tile: 4 d-atoms [64 tok x 128 B]
 // shared memory, offsets from the 1024-byte aligned base
 constexpr int kPfQ = 0;                                // Q: 4 k-atoms [128 rows x 128 B]
-constexpr int kPfK = kPfQ + 4 * kPfRows * 128;         // K tile FP16: 4 d-atoms [64 tok x 128 B]
-constexpr int kPfV = kPfK + 4 * kPfTok * 128;          // V tile FP16: same layout
+constexpr int kPfK = kPfQ + 4 * kPfRows * 128;         // two K tiles FP16
+constexpr int kPfV = kPfK + 2 * kPfTileBytes;          // one V tile FP16
 constexpr int kPfCodeBox = kPfTok * kCodeBytes;        // 8 KB
 constexpr int kPfScaleBox = kPfTok * kScaleBytes;      // 1 KB
 constexpr int kPfStage = kPfCodeBox + kPfScaleBox;     // 9 KB
-constexpr int kPfKRing = kPfV + 4 * kPfTok * 128;
+constexpr int kPfKRing = kPfV + kPfTileBytes;
 constexpr int kPfVRing = kPfKRing + kPfStages * kPfStage;
 constexpr int kPfBars = kPfVRing + kPfStages * kPfStage;
-// kfull[3] kempty[3] vfull[3] vempty[3] kready kfree sfull[2] sfree[2]
-// vready pready pvdone fin
-constexpr int kPfNumBars = 4 * kPfStages + 10;
+// kfull[3] kempty[3] vfull[3] vempty[3] kready[2] kfree[2] sfull[2]
+// sfree[2] vready pready pvdone fin
+constexpr int kPfNumBars = 4 * kPfStages + 12;
 constexpr int kPfMeta = kPfBars + 8 * kPfNumBars;      // TMEM base, abort flag
 constexpr int kPfRowfac = kPfMeta + 16;                // [128] row score factors
 constexpr int kPfPid = kPfRowfac + 4 * kPfRows;        // [kPfPidCache] page ids
@@ -85,9 +87,9 @@ enum PfBar : int {
   kBarKEmpty = kPfStages,
   kBarVFull = 2 * kPfStages,
   kBarVEmpty = 3 * kPfStages,
-  kBarKReady = 4 * kPfStages,
-  kBarKFree,
-  kBarSFull,  // two
+  kBarKReady = 4 * kPfStages,  // two (per K buffer)
+  kBarKFree = kBarKReady + 2,   // two
+  kBarSFull = kBarKFree + 2,    // two
   kBarSFree = kBarSFull + 2,  // two
   kBarVReady = kBarSFree + 2,
   kBarPReady,
@@ -153,7 +155,9 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       mbar_init(bar(kBarVEmpty + s), kPfDqWarps);
     }
     mbar_init(bar(kBarKReady), kPfDqWarps);
+    mbar_init(bar(kBarKReady + 1), kPfDqWarps);
     mbar_init(bar(kBarKFree), 1);
+    mbar_init(bar(kBarKFree + 1), 1);
     mbar_init(bar(kBarSFull), 1);
     mbar_init(bar(kBarSFull + 1), 1);
     mbar_init(bar(kBarSFree), kPfSoftWarps);
@@ -280,20 +284,21 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       constexpr uint32_t idesc_qk = tc::idesc_f16_f32(kPfRows, kPfTok);
       constexpr uint32_t idesc_pv = tc::idesc_f16_f32(kPfRows, kHeadDim, /*b_mn_major=*/true);
       const uint64_t dq = tc::smem_desc_k128(sb + kPfQ);
-      const uint64_t dk = tc::smem_desc_k128(sb + kPfK);
+      const uint64_t dk0 = tc::smem_desc_k128(sb + kPfK);
       const uint64_t dv = tc::smem_desc_mn128(sb + kPfV, kPfTok * 128, 1024);
       bool fine = true;
       auto qk = [&](int j) -> bool {
-        if (!mbar_wait(bar(kBarKReady), j & 1)) return false;
+        if (!mbar_wait(bar(kBarKReady + (j & 1)), (j >> 1) & 1)) return false;
         if (j >= 2 && !mbar_wait(bar(kBarSFree + (j & 1)), ((j - 2) >> 1) & 1)) return false;
         tc::fence_after();
         const uint32_t d = tbase + kPfTmS + 64u * (j & 1);
+        const uint64_t dk = dk0 + (uint64_t)(((j & 1) * kPfTileBytes) >> 4);
 #pragma unroll
         for (int ks = 0; ks < kHeadDim / 16; ++ks)
           tc::mma_ss(d, dq + (uint64_t)(((ks >> 2) * (kPfRows * 128) + (ks & 3) * 32) >> 4),
                      dk + (uint64_t)(((ks >> 2) * (kPfTok * 128) + (ks & 3) * 32) >> 4), idesc_qk, ks > 0);
         tc::commit(bar(kBarSFull + (j & 1)));
-        tc::commit(bar(kBarKFree));
+        tc::commit(bar(kBarKFree + (j & 1)));
         return true;
       };
       auto pv = [&](int j) -> bool {
@@ -321,35 +326,30 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       if (!mbar_wait(bar(kBarFin), 0)) flag_error(kErrTimeout);
     }
   } else if (warp >= kPfDq0) {
-    // -------------------------------------------------------------- dequant
-    const int t = (warp - kPfDq0) * 32 + lane;
-    const int tt = t >> 2, u = t & 3;  // token row of the tile, head-dim quarter
+    // ------------------------------------------------- dequant (K or V)
+    const bool is_k = warp < kPfDq0 + kPfDqWarps;
+    const int t = (warp - kPfDq0 - (is_k ? 0 : kPfDqWarps)) * 32 + lane;
+    const int tt = t >> 1, u0 = 2 * (t & 1);  // token row of the tile, first of two head-dim atoms
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
       const int s = i % kPfStages;
-      const uint32_t ph = (i / kPfStages) & 1;
       const bool stale = i * kPfTok + tt >= L;
-      ok &= mbar_wait(bar(kBarKFull + s), ph);
-      if (i > 0) ok &= mbar_wait(bar(kBarKFree), (i - 1) & 1);  // QK(i-1) has read the K buffer
-      if (__any_sync(kFull, !ok || *abort_flag)) break;          // the whole warp leaves together
-      const uint32_t kr = sb + kPfKRing + s * kPfStage;
-      pf_dequant_part(kr, kr + kPfCodeBox, sb + kPfK, tt, u, stale);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar(kBarKEmpty + s));
-        mbar_arrive(bar(kBarKReady));
+      ok &= mbar_wait(bar((is_k ? kBarKFull : kBarVFull) + s), (i / kPfStages) & 1);
+      if (is_k) {
+        if (i >= 2) ok &= mbar_wait(bar(kBarKFree + (i & 1)), ((i - 2) >> 1) & 1);  // QK(i-2) read the buffer
+      } else {
+        if (i >= 1) ok &= mbar_wait(bar(kBarPvDone), (i - 1) & 1);  // PV(i-1) read the V buffer
       }
-      ok &= mbar_wait(bar(kBarVFull + s), ph);
-      if (i > 0) ok &= mbar_wait(bar(kBarPvDone), (i - 1) & 1);  // PV(i-1) has read the V buffer
-      if (__any_sync(kFull, !ok || *abort_flag)) break;
-      const uint32_t vr = sb + kPfVRing + s * kPfStage;
-      pf_dequant_part(vr, vr + kPfCodeBox, sb + kPfV, tt, u, stale);
+      if (__any_sync(kFull, !ok || *abort_flag)) break;  // the whole warp leaves together
+      const uint32_t ring = sb + (is_k ? kPfKRing : kPfVRing) + s * kPfStage;
+      const uint32_t dst = sb + (is_k ? kPfK + (i & 1) * kPfTileBytes : kPfV);
+      pf_dequant_part(ring, ring + kPfCodeBox, dst, tt, u0, stale);
+      pf_dequant_part(ring, ring + kPfCodeBox, dst, tt, u0 + 1, stale);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(bar(kBarVEmpty + s));
-        mbar_arrive(bar(kBarVReady));
+        mbar_arrive(bar((is_k ? kBarKEmpty : kBarVEmpty) + s));
+        mbar_arrive(bar(is_k ? kBarKReady + (i & 1) : kBarVReady));
       }
     }
     if (__any_sync(kFull, !ok) && lane == 0) {
