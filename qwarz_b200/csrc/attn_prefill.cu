@@ -30,8 +30,10 @@
 //   QK(j)  S[128 rows x 64 tok] = Q K^T, A = Q (K-major in shared memory,
 //          rows scaled by a power of two so they convert to FP16 exactly),
 //          B = K(j); into one of two S buffers in TMEM;
-//   soft   base-2 online softmax per row; P in FP16 (the reference's PV
-//          operand precision) written to TMEM as the A operand of PV;
+//   soft   base-2 online softmax per row (packed f32x2 arithmetic; the
+//          mask only on tiles that cross a row's causal limit); P in FP16
+//          (the reference's PV operand precision) written to TMEM as the A
+//          operand of PV;
 //   PV(j)  O[128 x 256] += P V(j), A = P from TMEM, B = V(j) MN-major.
 // The MMA thread issues QK(j+1) ahead of PV(j).  Every wait
 // is bounded; a role that times out raises the abort flag and the others
@@ -122,6 +124,29 @@ QWZ_DEVINL void pf_dequant_part(uint32_t codes, uint32_t scales, uint32_t out, i
              hmul2_u32(hv[2], s2), hmul2_u32(hv[3], s2));
     }
   }
+}
+
+// Packed f32x2 arithmetic (one instruction for two lanes of work) and the
+// 3-input max.
+QWZ_DEVINL void pf_ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  uint64_t d;
+  asm("{\n .reg .b64 a, b, c;\n mov.b64 a, {%1, %2};\n mov.b64 b, {%3, %3};\n mov.b64 c, {%4, %4};\n"
+      " fma.rn.f32x2 %0, a, b, c;\n}\n"
+      : "=l"(d)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+QWZ_DEVINL void pf_fadd2(float& a0, float& a1, float b0, float b1) {
+  uint64_t d;
+  asm("{\n .reg .b64 a, b;\n mov.b64 a, {%1, %2};\n mov.b64 b, {%3, %4};\n add.rn.f32x2 %0, a, b;\n}\n"
+      : "=l"(d)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+  asm("mov.b64 {%0, %1}, %2;\n" : "=f"(a0), "=f"(a1) : "l"(d));
+}
+QWZ_DEVINL float pf_fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <int NC>
@@ -366,7 +391,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
     const int limit = valid ? pre + pos + 1 : 1;  // keys j < limit are visible
     const float fac = rowfac[r];
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-    float m_ref = -CUDART_INF_F, l = 0.f;
+    float m_ref = -CUDART_INF_F, la = 0.f, lb = 0.f;  // the row sum in two halves (packed adds)
     bool ok = true;
     int done = 0;
     for (int j = 0; j < n_tiles; ++j) {
@@ -388,23 +413,30 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       if (lane == 0) mbar_arrive(bar(kBarSFree + (j & 1)));  // QK(j+2) may overwrite this buffer
 
       const int t0 = j * kPfTok;
-      float mt = -CUDART_INF_F;
+      if (!__all_sync(kFull, t0 + kPfTok <= limit)) {  // a diagonal tile: keys past the row's limit
 #pragma unroll
-      for (int c = 0; c < kPfTok; ++c) {
-        x[c] = (t0 + c < limit) ? x[c] * fac : -CUDART_INF_F;
-        mt = fmaxf(mt, x[c]);
+        for (int c = 0; c < kPfTok; ++c) x[c] = (t0 + c < limit) ? x[c] : -CUDART_INF_F;
       }
+      // raw row max (fac > 0, so the scaled max is the max scaled)
+      float mr = -CUDART_INF_F;
+#pragma unroll
+      for (int c = 0; c < kPfTok; c += 2) mr = pf_fmax3(mr, x[c], x[c + 1]);
+      const float mt = mr * fac;
       // the row's reference max moves only by more than 2^kLazy
       const bool need = mt > m_ref + kLazy;
       const float m_new = need ? mt : m_ref;
       const float alpha = (need && m_ref != -CUDART_INF_F) ? exp2_approx(m_ref - m_new) : 1.f;
       const float mu = m_new == -CUDART_INF_F ? 0.f : m_new;
-      l *= alpha;
+      la *= alpha;
+      lb *= alpha;
       uint32_t pw[kPfTok / 2];
 #pragma unroll
       for (int c = 0; c < kPfTok / 2; ++c) {
-        const float p0 = exp2_approx(x[2 * c] - mu), p1 = exp2_approx(x[2 * c + 1] - mu);
-        l += p0 + p1;
+        float p0, p1;
+        pf_ffma2(p0, p1, x[2 * c], x[2 * c + 1], fac, -mu);  // base-2 score minus the reference max
+        p0 = exp2_approx(p0);
+        p1 = exp2_approx(p1);
+        pf_fadd2(la, lb, p0, p1);
         pw[c] = pack_half2(p0, p1);
       }
       m_ref = m_new;
@@ -450,6 +482,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
     tc::fence_after();
     {
       T* out = reinterpret_cast<T*>(p.out) + ((size_t)(valid ? pos : 0) * kQHeads + kvh * kGroup + r % kGroup) * kHeadDim;
+      const float l = la + lb;
       const float inv = (have_o && l > 0.f) ? 1.f / l : 0.f;
 #pragma unroll 1
       for (int c = 0; c < kHeadDim; c += 16) {
