@@ -100,32 +100,6 @@ enum PfBar : int {
 };
 static_assert(kBarFin + 1 == kPfNumBars, "barrier count");
 
-// Quarter u of token row tt of a tile (code chunks 2u, 2u+1 = head dim
-// 64u .. 64u+63, their four scales) -> FP16 row tt of head-dim atom u.
-// `zero` (a token at or past the sequence end) writes zeros.
-QWZ_DEVINL void pf_dequant_part(uint32_t codes, uint32_t scales, uint32_t out, int tt, int u, bool zero) {
-  uint32_t sc = lds32(scales + tt * kScaleBytes + 4 * u);
-  if (zero) sc = 0u;
-  uint32_t s01, s23;
-  e4m3x4_to_f16x2x2(sc, s01, s23);
-  const uint32_t sbc[4] = {__byte_perm(s01, 0, 0x1010), __byte_perm(s01, 0, 0x3232),
-                           __byte_perm(s23, 0, 0x1010), __byte_perm(s23, 0, 0x3232)};
-  const uint32_t row = out + u * (kPfTok * 128) + tt * 128;
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint4 w = lds128(codes + tt * kCodeBytes + (((2 * u + h) ^ (tt & 7)) << 4));
-    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint32_t hv[4];
-      e2m1x8_to_f16x2x4(wv[j], hv);
-      const uint32_t s2 = sbc[2 * h + (j >> 1)];
-      sts128(row + (((4 * h + j) ^ (tt & 7)) << 4), hmul2_u32(hv[0], s2), hmul2_u32(hv[1], s2),
-             hmul2_u32(hv[2], s2), hmul2_u32(hv[3], s2));
-    }
-  }
-}
-
 // Packed f32x2 arithmetic (one instruction for two lanes of work) and the
 // 3-input max.
 QWZ_DEVINL void pf_ffma2(float& d0, float& d1, float a0, float a1, float b, float c) {
@@ -147,6 +121,35 @@ QWZ_DEVINL float pf_fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// Half u0/2 of token row tt (head-dim atoms u0 and u0 + 1: code chunks
+// 2u0 .. 2u0+3, scales 4u0 .. 4u0+7) -> FP16.  Every shared-memory load is
+// issued before the first convert, so their latencies overlap.
+QWZ_DEVINL void pf_dequant_half(uint32_t codes, uint32_t scales, uint32_t out, int tt, int u0, bool zero) {
+  uint32_t s0, s1;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(s0), "=r"(s1) : "r"(scales + tt * kScaleBytes + 4 * u0));
+  uint4 w[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) w[c] = lds128(codes + tt * kCodeBytes + (((2 * u0 + c) ^ (tt & 7)) << 4));
+  if (zero) s0 = s1 = 0u;
+  uint32_t h[4];
+  e4m3x4_to_f16x2x2(s0, h[0], h[1]);
+  e4m3x4_to_f16x2x2(s1, h[2], h[3]);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {  // code chunk 2u0 + c: head dim 32 (2u0 + c) .. +31
+    const uint32_t wv[4] = {w[c].x, w[c].y, w[c].z, w[c].w};
+    const uint32_t row = out + (u0 + (c >> 1)) * (kPfTok * 128) + tt * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // 8 values: scale 2c + j / 2 of the eight
+      const int b = 2 * c + (j >> 1);
+      const uint32_t s2 = __byte_perm(h[b >> 1], 0, (b & 1) ? 0x3232 : 0x1010);
+      uint32_t hv[4];
+      e2m1x8_to_f16x2x4(wv[j], hv);
+      sts128(row + (((4 * (c & 1) + j) ^ (tt & 7)) << 4), hmul2_u32(hv[0], s2), hmul2_u32(hv[1], s2),
+             hmul2_u32(hv[2], s2), hmul2_u32(hv[3], s2));
+    }
+  }
 }
 
 template <int NC>
@@ -368,8 +371,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       if (__any_sync(kFull, !ok || *abort_flag)) break;  // the whole warp leaves together
       const uint32_t ring = sb + (is_k ? kPfKRing : kPfVRing) + s * kPfStage;
       const uint32_t dst = sb + (is_k ? kPfK + (i & 1) * kPfTileBytes : kPfV);
-      pf_dequant_part(ring, ring + kPfCodeBox, dst, tt, u0, stale);
-      pf_dequant_part(ring, ring + kPfCodeBox, dst, tt, u0 + 1, stale);
+      pf_dequant_half(ring, ring + kPfCodeBox, dst, tt, u0, stale);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
