@@ -499,6 +499,57 @@ def run_extra(args, device) -> dict:
                 "windowed_verify_us": ms_w * 1e3, "speedup_vs_windows": ms_w / ms}
             del c, perm
             torch.cuda.empty_cache()
+        # draft-model prefill (SURVEY next item 3): FP16 K/V read in place vs
+        # the reference's torch route for the same shapes (draft.py:33-86:
+        # SDPA causal when S == T, else the LSE merge of two flash calls)
+        from qwarz_b200.draft_attention import draft_attend
+        for pre, S in ((0, 8192), (61440, 4096)):
+            T = pre + S
+            qd = torch.randn(1, S, HEADS, DIM, generator=g, device=device).half()
+            kd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
+            vd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
+            outd = torch.empty_like(qd)
+
+            def ours():
+                ops.draft_prefill(qd, kd, vd, outd, DIM ** -0.5)
+
+            expand = [False]  # GQA through the flash op, else heads repeated first
+
+            def sdpa_route():
+                qt, kt, vt = qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2)
+                if pre == 0:
+                    o = torch.nn.functional.scaled_dot_product_attention(
+                        qt, kt, vt, is_causal=True, scale=DIM ** -0.5, enable_gqa=True)
+                else:
+                    if expand[0]:
+                        kt = kt.repeat_interleave(HEADS // KV_HEADS, 1)
+                        vt = vt.repeat_interleave(HEADS // KV_HEADS, 1)
+                    op = torch.ops.aten._scaled_dot_product_flash_attention
+                    o1, l1, *_ = op(qt, kt[:, :, :pre], vt[:, :, :pre], 0.0, False, False, scale=DIM ** -0.5)
+                    o2, l2, *_ = op(qt, kt[:, :, pre:], vt[:, :, pre:], 0.0, True, False, scale=DIM ** -0.5)
+                    a, b = l1.unsqueeze(-1), l2.unsqueeze(-1)
+                    tot = torch.logaddexp(a, b)
+                    o = (o1.float() * (a - tot).exp() + o2.float() * (b - tot).exp()).half()
+                return o.transpose(1, 2).contiguous()
+
+            for _ in range(2):
+                ours()
+            ms = cuda_time(ours, 5, stream) / 5
+            try:
+                sdpa_route()
+            except RuntimeError:
+                expand[0] = True
+            for _ in range(2):
+                sdpa_route()
+            ms_ref = cuda_time(sdpa_route, 3, stream) / 3
+            flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
+            res["configs"][f"draft_prefill_{pre}+{S}"] = {
+                "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+                "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
+                "torch_sdpa_route_us": ms_ref * 1e3, "sdpa_heads_repeated": expand[0],
+                "speedup_vs_sdpa_route": ms_ref / ms}
+            del qd, kd, vd, outd
+            torch.cuda.empty_cache()
     if args.workload in ("c4", "all"):
         res["configs"]["c4_262144_1gpu"] = nvfp4_config(262144, 1, 16)
     if args.workload in ("c5", "all"):
@@ -545,6 +596,21 @@ def run_profile_case(args, device) -> dict:
     build.build()
     tokens, pages = 65536, 256
     g = torch.Generator(device=device).manual_seed(11)
+    if args.workload == "profile_prefill":
+        # one NVFP4 prefill (8,192 rows onto an empty cache) then one draft
+        # prefill of the same shape: 9.4 MB of pages, 100 MB of Q and of O
+        S = 8192
+        cache, perm = build_layer(ops, device, S // PAGE, S, seed=2)
+        q = torch.randn(S, HEADS, DIM, generator=g, device=device).bfloat16()
+        out = torch.empty_like(q)
+        pre = torch.zeros(1, dtype=torch.int32, device=device)
+        ops.nvfp4_prefill(q, cache[0], cache[1], cache[2], cache[3], perm, pre, out)
+        qd = q.half()[None]
+        kd = torch.randn(1, S, KV_HEADS, DIM, generator=g, device=device).half()
+        vd = torch.randn(1, S, KV_HEADS, DIM, generator=g, device=device).half()
+        ops.draft_prefill(qd, kd, vd, torch.empty_like(qd))
+        torch.cuda.synchronize()
+        return {"workload": args.workload, "tokens": S, "ok": True}
     if args.workload == "profile_draft":
         T = tokens + 6
         k8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
@@ -648,7 +714,7 @@ def main():
                          "rank can reach every GPU, else NCCL)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c3", "c4", "c5", "prefill", "all", "profile_decode",
+                    choices=["auto", "c3", "c4", "c5", "prefill", "all", "profile_prefill", "profile_decode",
                              "profile_verify", "profile_draft"],
                     help="auto: the driver's headline (C2 at N=1, weak-scaled sharding at N>1); "
                          "c3/c4/c5/all: the other BASELINE configs on one GPU (separate JSON); "

@@ -146,6 +146,20 @@ int qwz_nvfp4_prefill(const void* q, const void* k_cache, const void* v_cache, c
                       int32_t dtype, void* stream);
 
 /*
+ * Draft-model prefill attention over FP16 K/V rows (no pages, no
+ * quantisation): q [q_len, 24, 256] FP16, k and v [kv_len, 4, 256] FP16 with
+ * a token stride of k_token_stride / v_token_stride elements (a multiple of
+ * 8, >= 1024; head and dim contiguous), out [q_len, 24, 256] FP16.  Query
+ * row s sees keys j <= kv_len - q_len + s (bottom-right causal), GQA 6.
+ * Replaces engine/forward/draft.py:33-61 `draft_attend` (SDPA for short
+ * chunks, `_merge_bottom_right` for a chunk after a past, and the FP8
+ * repage + sm120 paged FMHA of draft.py:99-181 for long ones).  Requires
+ * 1 <= q_len <= kv_len.  No workspace.
+ */
+int qwz_draft_prefill(const void* q, const void* k, const void* v, void* out, int32_t q_len, int32_t kv_len,
+                      int64_t k_token_stride, int64_t v_token_stride, float sm_scale, void* stream);
+
+/*
  * qwz_nvfp4_attend without a caller-supplied workspace.  No counterpart in
  * the reference: it exists for callers that cannot allocate device memory
  * (an engine that owns every allocation, a fixed memory pool, an FFI that

@@ -33,6 +33,7 @@ SIGNATURES = {
     "qwz_nvfp4_attend": [c_void_p] * 12 + [c_int32] * 4 + [c_float, c_int32, c_void_p],
     "qwz_nvfp4_attend_noalloc": [c_void_p] * 10 + [c_int32] * 4 + [c_float, c_int32, c_void_p],
     "qwz_nvfp4_prefill": [c_void_p] * 8 + [c_int32] * 3 + [c_float, c_int32, c_void_p],
+    "qwz_draft_prefill": [c_void_p] * 4 + [c_int32] * 2 + [c_int64] * 2 + [c_float, c_void_p],
     "qwz_attn_shard_partial": [c_void_p] * 10 + [c_int32] * 6 + [c_float, c_int32, c_void_p],
     "qwz_lse_combine_gathered": [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p],
     "qwz_fp8_draft_decode": [c_void_p] * 9 + [c_int32, c_int32, c_void_p],

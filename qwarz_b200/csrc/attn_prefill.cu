@@ -38,6 +38,12 @@
 // The MMA thread issues QK(j+1) ahead of PV(j).  Every wait
 // is bounded; a role that times out raises the abort flag and the others
 // leave at their next wait.
+//
+// The same kernel, instantiated with kDense, is the draft model's prefill
+// (engine/forward/draft.py:33-61 `draft_attend`: bottom-right causal
+// attention of q_len FP16 rows over an FP16 K/V of kv_len rows, which the
+// reference runs as SDPA, or as an FP8 repage + sm120 paged FMHA for long
+// chunks, draft.py:99-181).  Here the K and V rows are read in place.
 
 #include "attn_common.cuh"
 #include "tc_common.cuh"
@@ -79,6 +85,7 @@ static_assert(kPfKRing % 1024 == 0 && kPfVRing % 1024 == 0 && kPfStage % 1024 ==
               "TMA destinations with the 128-byte swizzle are 1024-byte aligned");
 static_assert(kPfBars % 8 == 0 && kPfRowfac % 16 == 0 && kPfPid % 4 == 0, "alignment");
 static_assert(kPfSmem <= 227 * 1024, "shared memory");
+static_assert(kPfV + 2 * kPfTileBytes <= kPfBars, "dense source: the second V tile reuses the code rings");
 // tensor-memory columns: S buffers 0 and 1, P (FP16 pairs), O
 constexpr uint32_t kPfTmS = 0, kPfTmP = 128, kPfTmO = 256, kPfTmCols = 512;
 
@@ -160,8 +167,13 @@ QWZ_DEVINL void pf_regs_ready(float (&v)[NC]) {
 
 }  // namespace
 
-template <typename T>
-__global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const __grid_constant__ PrefillParams p) {
+// kDense = false: the NVFP4 paged cache (dequant warps 6-13).
+// kDense = true: FP16 K, V [kv_len, 4, 256] rows (the draft model's cache);
+// the producer's TMA writes the tiles straight into the FP16 operand layout,
+// K and V both double-buffered, and warps 6-13 are not launched.
+template <typename T, bool kDense>
+__global__ void __launch_bounds__(kPfWarps * 32, 1) prefill_attn_kernel(const __grid_constant__ PrefillParams p) {
+  constexpr int kWarps = kDense ? kPfDq0 : kPfWarps;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sraw = smem_u32(smem);
   const uint32_t sb = (sraw + 1023u) & ~1023u;
@@ -175,15 +187,17 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
   int* pid = reinterpret_cast<int*>(sg + kPfPid);
 
   if (tid == 0) {
+    // dense: KReady[b] / VFull[b] complete on the TMA bytes, VEmpty[b] on
+    // the PV commit that read V buffer b
 #pragma unroll
     for (int s = 0; s < kPfStages; ++s) {
       mbar_init(bar(kBarKFull + s), 1);
-      mbar_init(bar(kBarKEmpty + s), kPfDqWarps);
+      mbar_init(bar(kBarKEmpty + s), kDense ? 1 : kPfDqWarps);
       mbar_init(bar(kBarVFull + s), 1);
-      mbar_init(bar(kBarVEmpty + s), kPfDqWarps);
+      mbar_init(bar(kBarVEmpty + s), kDense ? 1 : kPfDqWarps);
     }
-    mbar_init(bar(kBarKReady), kPfDqWarps);
-    mbar_init(bar(kBarKReady + 1), kPfDqWarps);
+    mbar_init(bar(kBarKReady), kDense ? 1 : kPfDqWarps);
+    mbar_init(bar(kBarKReady + 1), kDense ? 1 : kPfDqWarps);
     mbar_init(bar(kBarKFree), 1);
     mbar_init(bar(kBarKFree + 1), 1);
     mbar_init(bar(kBarSFull), 1);
@@ -203,7 +217,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
   }
   griddep_wait();  // barriers and tensor memory are set up while the previous kernel drains
 
-  const int pre = __ldg(p.seqlens);
+  const int pre = kDense ? p.pre_len : __ldg(p.seqlens);
   const int S = p.q_len;
   const int L = pre + S;                          // post-append length
   const int pos0 = blk * kPfPos;
@@ -212,14 +226,16 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
   const int n_tiles = (lim_max + kPfTok - 1) / kPfTok;
 
   // the pages of the tiles, staged once
-  const int n_pg = min((lim_max + kPage - 1) / kPage, min(p.table_width, kPfPidCache));
-  for (int i = tid; i < n_pg; i += kPfWarps * 32) {
-    const int pp = __ldg(p.block_table + i);
-    pid[i] = (pp >= 0 && pp < p.num_pages) ? pp : -1;
+  if constexpr (!kDense) {
+    const int n_pg = min((lim_max + kPage - 1) / kPage, min(p.table_width, kPfPidCache));
+    for (int i = tid; i < n_pg; i += kWarps * 32) {
+      const int pp = __ldg(p.block_table + i);
+      pid[i] = (pp >= 0 && pp < p.num_pages) ? pp : -1;
+    }
   }
   // Q rows -> K-major FP16 operand, row r = (position r / 6, head r % 6),
   // scaled by a power of two (exact for BF16 and FP16 inputs)
-  for (int r = warp; r < kPfRows; r += kPfWarps) {
+  for (int r = warp; r < kPfRows; r += kWarps) {
     const int pos = pos0 + r / kGroup;
     const bool valid = r < kGroup * kPfPos && pos < S;
     uint32_t w[4] = {0u, 0u, 0u, 0u};
@@ -256,7 +272,51 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
   tc::fence_after();
   const uint32_t tbase = *reinterpret_cast<volatile uint32_t*>(sg + kPfMeta);
 
-  if (warp == kPfProd) {
+  if (kDense && warp == kPfProd) {
+    // ------------------------------------- TMA producer, dense FP16 rows
+    // tile i -> K buffer i & 1 and V buffer i & 1: four boxes of 64 tokens
+    // x 128 B (64 head dims) each, 128-byte swizzle = the operand layout.
+    // Rows past kv_len read as zeros.
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&p.tm_kc);
+      tma_prefetch_desc(&p.tm_vc);
+      int issued_k = 0, issued_v = 0;
+      for (int i = 0; i < n_tiles; ++i) {
+        const int b = i & 1;
+        const uint32_t ph = ((i - 2) >> 1) & 1;
+        if (*abort_flag) break;
+        if (i >= 2 && !mbar_wait(bar(kBarKFree + b), ph)) {  // QK(i-2) read K buffer b
+          flag_error(kErrTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t kr = bar(kBarKReady + b);
+        mbar_arrive_expect_tx(kr, kPfTileBytes);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_2d(sb + kPfK + b * kPfTileBytes + a * (kPfTok * 128), &p.tm_kc,
+                      kvh * (kHeadDim * 2) + a * 128, i * kPfTok, kr);
+        issued_k = i + 1;
+        if (i >= 2 && !mbar_wait(bar(kBarVEmpty + b), ph)) {  // PV(i-2) read V buffer b
+          flag_error(kErrTimeout);
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t vr = bar(kBarVFull + b);
+        mbar_arrive_expect_tx(vr, kPfTileBytes);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tma_load_2d(sb + kPfV + b * kPfTileBytes + a * (kPfTok * 128), &p.tm_vc,
+                      kvh * (kHeadDim * 2) + a * 128, i * kPfTok, vr);
+        issued_v = i + 1;
+      }
+      // never leave with copies in flight (only reachable after an abort)
+      for (int i = max(issued_k - 2, 0); i < issued_k; ++i)
+        if (!mbar_wait(bar(kBarKReady + (i & 1)), (i >> 1) & 1)) flag_error(kErrTimeout);
+      for (int i = max(issued_v - 2, 0); i < issued_v; ++i)
+        if (!mbar_wait(bar(kBarVFull + (i & 1)), (i >> 1) & 1)) flag_error(kErrTimeout);
+    }
+  } else if (warp == kPfProd) {
     // -------------------------------------------------------- TMA producer
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&p.tm_kc);
@@ -330,13 +390,17 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
         return true;
       };
       auto pv = [&](int j) -> bool {
-        if (!mbar_wait(bar(kBarPReady), j & 1) || !mbar_wait(bar(kBarVReady), j & 1)) return false;
+        if (!mbar_wait(bar(kBarPReady), j & 1)) return false;
+        if (kDense ? !mbar_wait(bar(kBarVFull + (j & 1)), (j >> 1) & 1) : !mbar_wait(bar(kBarVReady), j & 1))
+          return false;
         tc::fence_after();
+        const uint64_t dvj = kDense ? dv + (uint64_t)(((j & 1) * kPfTileBytes) >> 4) : dv;
 #pragma unroll
         for (int kk = 0; kk < kPfTok / 16; ++kk)
-          tc::mma_ts(tbase + kPfTmO, tbase + kPfTmP + 8u * kk, dv + (uint64_t)((kk * 2048) >> 4), idesc_pv,
+          tc::mma_ts(tbase + kPfTmO, tbase + kPfTmP + 8u * kk, dvj + (uint64_t)((kk * 2048) >> 4), idesc_pv,
                      (j > 0 || kk > 0) ? 1u : 0u);
         tc::commit(bar(kBarPvDone));
+        if (kDense) tc::commit(bar(kBarVEmpty + (j & 1)));
         return true;
       };
       fine = qk(0);
@@ -353,7 +417,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
       tc::commit(bar(kBarFin));
       if (!mbar_wait(bar(kBarFin), 0)) flag_error(kErrTimeout);
     }
-  } else if (warp >= kPfDq0) {
+  } else if (!kDense && warp >= kPfDq0) {
     // ------------------------------------------------- dequant (K or V)
     const bool is_k = warp < kPfDq0 + kPfDqWarps;
     const int t = (warp - kPfDq0 - (is_k ? 0 : kPfDqWarps)) * 32 + lane;
@@ -523,11 +587,20 @@ __global__ void __launch_bounds__(kPfWarps * 32, 1) nvfp4_prefill_kernel(const _
 
 cudaError_t launch_nvfp4_prefill(const PrefillParams& p, int dtype, cudaStream_t stream) {
   if (p.q_len <= 0) return cudaSuccess;
-  auto kernel = dtype == kDtypeBF16 ? nvfp4_prefill_kernel<__nv_bfloat16> : nvfp4_prefill_kernel<__half>;
+  auto kernel = dtype == kDtypeBF16 ? prefill_attn_kernel<__nv_bfloat16, false> : prefill_attn_kernel<__half, false>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
   if (e != cudaSuccess) return e;
   const dim3 grid((unsigned)((p.q_len + kPfPos - 1) / kPfPos), kKvHeads);
   return launch_pdl(kernel, grid, dim3(kPfWarps * 32), kPfSmem, stream, p);
+}
+
+cudaError_t launch_draft_prefill(const PrefillParams& p, cudaStream_t stream) {
+  if (p.q_len <= 0) return cudaSuccess;
+  auto kernel = prefill_attn_kernel<__half, true>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)((p.q_len + kPfPos - 1) / kPfPos), kKvHeads);
+  return launch_pdl(kernel, grid, dim3(kPfDq0 * 32), kPfSmem, stream, p);
 }
 
 }  // namespace qwz

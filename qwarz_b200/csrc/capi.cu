@@ -77,12 +77,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D uint8 view [rows, row_bytes] of a pool, box box_x bytes x box_y rows.
-int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_x,
-              uint32_t box_y, CUtensorMapSwizzle swizzle) {
+// Rows of `inner_bytes` used bytes at a stride of `row_stride` bytes.
+int encode_rows(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_t row_stride, uint64_t rows,
+                uint32_t box_x, uint32_t box_y, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return fail(QWZ_ELAUNCH, "cuTensorMapEncodeTiled is unavailable from the driver");
-  cuuint64_t dims[2] = {row_bytes, rows};
-  cuuint64_t strides[1] = {row_bytes};
+  cuuint64_t dims[2] = {inner_bytes, rows};
+  cuuint64_t strides[1] = {row_stride};
   cuuint32_t box[2] = {box_x, box_y};
   cuuint32_t elem[2] = {1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
@@ -90,6 +91,11 @@ int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t row
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(QWZ_EINVAL, "TMA descriptor encoding failed (base, stride or extent)");
   return QWZ_OK;
+}
+
+int encode_2d(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint32_t box_x,
+              uint32_t box_y, CUtensorMapSwizzle swizzle) {
+  return encode_rows(m, base, row_bytes, row_bytes, rows, box_x, box_y, swizzle);
 }
 
 // Descriptors of the NVFP4 pool: codes [P*256, 512 B] (boxes of one head's
@@ -350,6 +356,33 @@ int qwz_nvfp4_prefill(const void* q, const void* k_cache, const void* v_cache, c
   if (!rc) rc = encode_2d(&p.tm_vs, v_scales, qwz::kRowBytesScales, rows, qwz::kScaleBytes, 64u, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   return launched(qwz::launch_nvfp4_prefill(p, dtype, as_stream(stream)), "qwz_nvfp4_prefill");
+}
+
+int qwz_draft_prefill(const void* q, const void* k, const void* v, void* out, int32_t q_len, int32_t kv_len,
+                      int64_t k_token_stride, int64_t v_token_stride, float sm_scale, void* stream) {
+  if (!q || !aligned(q, 16) || !out || !aligned(out, 16))
+    return fail(QWZ_EINVAL, "q and out must be non-null 16-byte aligned pointers");
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16)) return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+  if (q_len < 1 || kv_len < q_len) return fail(QWZ_EINVAL, "need 1 <= q_len <= kv_len");
+  const int64_t row = (int64_t)qwz::kKvHeads * qwz::kHeadDim;
+  if (k_token_stride < row || v_token_stride < row || k_token_stride % 8 || v_token_stride % 8 ||
+      k_token_stride > (int64_t(1) << 36) || v_token_stride > (int64_t(1) << 36))
+    return fail(QWZ_EINVAL, "token strides must be multiples of 8 elements and at least 1024");
+  if (!(sm_scale > 0.f) || !std::isfinite(sm_scale)) return fail(QWZ_EINVAL, "sm_scale must be positive and finite");
+  qwz::PrefillParams p{};
+  p.q = q;
+  p.out = out;
+  p.q_len = q_len;
+  p.pre_len = kv_len - q_len;
+  p.sm_scale_log2 = sm_scale * kLog2e;
+  // FP16 rows as bytes: [kv_len rows, 2048 B used of the stride], boxes of
+  // 128 B (64 head dims) x 64 tokens with the 128-byte swizzle
+  int rc = encode_rows(&p.tm_kc, k, (uint64_t)row * 2, (uint64_t)k_token_stride * 2, (uint64_t)kv_len, 128u, 64u,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = encode_rows(&p.tm_vc, v, (uint64_t)row * 2, (uint64_t)v_token_stride * 2, (uint64_t)kv_len, 128u, 64u,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  return launched(qwz::launch_draft_prefill(p, as_stream(stream)), "qwz_draft_prefill");
 }
 
 int qwz_attn_shard_partial(const void* q, const void* k_cache, const void* v_cache,

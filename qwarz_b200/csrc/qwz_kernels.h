@@ -49,7 +49,9 @@ struct alignas(64) SplitParams {
 
 // NVFP4 paged prefill attention (attn_prefill.cu): q [q_len, 24, 256] over
 // the post-append cache, lower-right causal.  Tensor maps as SplitParams
-// but with 64-row boxes.
+// but with 64-row boxes.  The dense FP16 source (draft prefill) uses tm_kc /
+// tm_vc over K, V [kv_len rows, token stride] with 128-byte x 64-row boxes,
+// pre_len instead of seqlens, and no table.
 struct alignas(64) PrefillParams {
   CUtensorMap tm_kc, tm_vc, tm_ks, tm_vs;
   const void* q;                 // [q_len, 24, 256] FP16/BF16
@@ -60,6 +62,7 @@ struct alignas(64) PrefillParams {
   int num_pages;
   int q_len;
   float sm_scale_log2;
+  int pre_len;                   // dense FP16 source: keys before the q_len rows (host)
 };
 
 // LSE combine of split partials.  Row r, split s reads
@@ -131,6 +134,7 @@ struct ExchangeParams {
 
 cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_nvfp4_prefill(const PrefillParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_draft_prefill(const PrefillParams& p, cudaStream_t stream);
 cudaError_t launch_shard_exchange(const ExchangeParams& p, int emulated, int dtype, cudaStream_t stream);
 cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream);
 cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStream_t stream);

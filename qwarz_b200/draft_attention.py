@@ -1,4 +1,13 @@
-"""One-row decode attention for the MTP proposer over the FP8 shadow KV.
+"""Draft-model attention for the MTP proposer.
+
+`draft_attend` is the drop-in for engine/forward/draft.py:33-61: q_len new
+FP16 rows over the draft's FP16 K/V (bottom-right causal, GQA 6) in one
+sm_100a launch that reads K and V in place, for every q_len.  The reference
+picks SDPA, an LSE merge of two SDPA calls, or an FP8 repage + sm120 paged
+FMHA (draft.py:99-181) by size; the result here is the FP32-softmax value
+all three approximate.
+
+One-row decode attention over the FP8 shadow KV follows.
 
 Drop-in for engine/forward/draft_attention.py:82-108 (`DecodeAttention`):
 the constructor allocates the split workspace once and `attend` launches the
@@ -17,6 +26,18 @@ from . import ops
 SPLITS = 37   # 37 splits x 4 KV heads = 148 CTAs, one per SM
 KV_HEADS = 4
 DIM = 256
+
+
+def draft_attend(query, key, value):
+    """query [1, S, 24, 256] FP16; key, value [1, T, 4, 256] FP16 (T >= S;
+    head and dim contiguous, e.g. a [:, :T] view of the preallocated draft
+    cache) -> [1, S, 24, 256] FP16, row s attending keys j <= T - S + s."""
+    if query.dim() != 4 or query.shape[0] != 1:
+        raise ValueError("query must be [1, S, 24, 256]")
+    q = query if query.is_contiguous() else query.contiguous()
+    out = torch.empty_like(q)
+    ops.draft_prefill(q, key, value, out, DIM ** -0.5)
+    return out
 
 
 class DecodeAttention:

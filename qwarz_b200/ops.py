@@ -235,6 +235,38 @@ def nvfp4_prefill(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_se
         _dtype_code(q.dtype), _stream(dev)), "qwz_nvfp4_prefill")
 
 
+def draft_prefill(q, k, v, out, sm_scale: float = DIM ** -0.5) -> None:
+    """Bottom-right causal attention of q [.., S, 24, 256] FP16 over FP16
+    k, v [.., T, 4, 256] (T >= S; head and dim contiguous, any token stride
+    that is a multiple of 8): query row s sees keys j <= T - S + s.  Writes
+    out (same shape as q)."""
+    dev = _cuda(q, k, v, out)
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.dtype != torch.float16:
+            raise ValueError(f"{name} must be FP16 (the draft model's dtype)")
+    _contig("q", q)
+    _contig("out", out)
+    if out.numel() != q.numel() or q.shape[-2:] != (HEADS, DIM):
+        raise ValueError("q and out must be [.., S, 24, 256]")
+    S = q.numel() // (HEADS * DIM)
+    rows = []
+    for name, t in (("k", k), ("v", v)):
+        if t.shape[-2:] != (KV_HEADS, DIM) or t.stride(-1) != 1 or t.stride(-2) != DIM:
+            raise ValueError(f"{name} must be [.., T, 4, 256] with head and dim contiguous")
+        if any(d != 1 for d in t.shape[:-3]):
+            raise ValueError(f"{name} must hold one sequence")
+        rows.append((t.shape[-3], t.stride(-3)))
+    (T, k_stride), (Tv, v_stride) = rows
+    if Tv != T:
+        raise ValueError("k and v must have the same number of rows")
+    if not 1 <= S <= T:
+        raise ValueError("need 1 <= q rows <= k rows (bottom-right causal)")
+    lib = _lib.load()
+    _lib.check(lib.qwz_draft_prefill(
+        _p(q), _p(k), _p(v), _p(out), S, T, k_stride, v_stride, float(sm_scale), _stream(dev)),
+        "qwz_draft_prefill")
+
+
 def shard_partial(q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
                   partial_o, partial_ml, send_buf, tok_begin: int, tok_span: int,
                   num_splits: int, sm_scale: float = DIM ** -0.5) -> None:
