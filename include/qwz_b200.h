@@ -274,6 +274,18 @@ int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const fl
                          void* out, int32_t splits, int32_t capacity, void* stream);
 
 /*
+ * One draft step with the FP8 shadow write fused in: what
+ * qwz_fp8_shadow_write(k_new, v_new, k8, v8, k_scale, v_scale, position)
+ * followed by qwz_fp8_draft_decode(...) computes, in two launches instead of
+ * three (engine/forward/draft.py:359-366 then draft_attention.py:82-108).
+ * k_new, v_new FP16 [4, 256]; position int32 [1] on the device, in
+ * [0, capacity) (a slot past length is written but not attended).
+ */
+int qwz_fp8_draft_step(const void* q, const void* k_new, const void* v_new, const int32_t* position, void* k8,
+                       void* v8, const float* k_scale, const float* v_scale, const int32_t* length, float* part,
+                       float* stat, void* out, int32_t splits, int32_t capacity, void* stream);
+
+/*
  * FP8 shadow write (replaces engine/forward/draft.py:359-366): writes one new
  * row k, v [4, 256] (FP16/BF16) into k8, v8 at slot position[0] as
  * E4M3(clamp(x / scale, +-448)), scale per (page, head) or 1 when NULL.

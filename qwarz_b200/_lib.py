@@ -37,6 +37,7 @@ SIGNATURES = {
     "qwz_attn_shard_partial": [c_void_p] * 10 + [c_int32] * 6 + [c_float, c_int32, c_void_p],
     "qwz_lse_combine_gathered": [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p],
     "qwz_fp8_draft_decode": [c_void_p] * 9 + [c_int32, c_int32, c_void_p],
+    "qwz_fp8_draft_step": [c_void_p] * 12 + [c_int32, c_int32, c_void_p],
     "qwz_fp8_shadow_write": [c_void_p] * 7 + [c_int32, c_int32, c_void_p],
     "qwz_nvfp4_gather": [c_void_p] * 5 + [c_int32] * 6 + [c_void_p],
     "qwz_peer_buffer_bytes": [c_int32, c_int32],

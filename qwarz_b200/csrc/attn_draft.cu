@@ -20,8 +20,16 @@
 //       128 + 16g + {0..15}); tokens are paired with prmt before the convert.
 // The K scale multiplies S, the V scale multiplies P (FP16, as the
 // reference's Triton draft kernel feeds its PV dot).
+//
+// Fused shadow write (qwz_fp8_draft_step): the new FP16 K/V row for store
+// slot app_slot[0] (engine/forward/draft.py:359-366, done there by two
+// index_copy_ before the attention) is converted by the warp that owns the
+// slot's row in its stage, right after the stage lands: it writes the E4M3
+// bytes to the store and over the stale row in shared memory, so one launch
+// replaces the write kernel and the attention reads the new row.
 
 #include "attn_common.cuh"
+#include "nvfp4_quant.cuh"
 
 namespace qwz {
 
@@ -79,6 +87,25 @@ QWZ_DEVINL void load_q_draft(const __half* q, int row, int qd, float sm_scale_lo
   cf1 = __shfl_sync(0xffffffffu, rowfac, 4 * (2 * qd + 1));
 }
 
+// Lane l's 8 bytes (d = 8l..8l+7) of the new K and V rows of head kvh at
+// store slot `slot`: into the store and, when stage != 0, over row r of that
+// shared-memory stage (half l / 16, 16-byte chunk (l % 16) / 2).
+QWZ_DEVINL void fp8_shadow_patch(const SplitParams& p, int slot, int kvh, int lane, float ks, float vs,
+                                 uint32_t stage, int r) {
+  const __half* kn = reinterpret_cast<const __half*>(p.app_k) + kvh * kHeadDim + 8 * lane;
+  const __half* vn = reinterpret_cast<const __half*>(p.app_v) + kvh * kHeadDim + 8 * lane;
+  const uint2 kb = quant::fp8_shadow8<__half>(kn, ks);
+  const uint2 vb = quant::fp8_shadow8<__half>(vn, vs);
+  const size_t off = ((size_t)slot * kKvHeads + kvh) * kHeadDim + 8 * lane;
+  *reinterpret_cast<uint2*>(const_cast<uint8_t*>(p.k_codes) + off) = kb;
+  *reinterpret_cast<uint2*>(const_cast<uint8_t*>(p.v_codes) + off) = vb;
+  if (stage != 0u) {
+    const uint32_t a = stage + (lane >> 4) * kDrHalf + swz128(r, (lane & 15) >> 1) + 8 * (lane & 1);
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};\n" ::"r"(a), "r"(kb.x), "r"(kb.y) : "memory");
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};\n" ::"r"(a + 2 * kDrHalf), "r"(vb.x), "r"(vb.y) : "memory");
+  }
+}
+
 QWZ_DEVINL void issue_stage(const SplitParams& p, DrMeta* meta, const StageRange& rg, int k, int slot,
                             uint32_t sbase, uint32_t bar_full, int kvh) {
   const int t0 = p.tok_begin + (rg.st_lo + k) * kDrTokens;
@@ -121,6 +148,21 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
   }
   griddep_wait();  // shared-memory set-up overlaps the previous kernel
   const StageRange rg = stage_range<kDrTokens>(p, split);
+  int slot_new = -1;  // fused shadow write: the store slot, while a stage of this CTA may hold it
+  if (p.app_k != nullptr) {
+    slot_new = __ldg(p.app_slot);
+    if (slot_new < 0 || slot_new >= p.capacity) {
+      if (split == 0 && kvh == 0 && tid == 0) flag_error(kErrSlotRange);
+      slot_new = -1;
+    } else if (slot_new >= rg.tok_end) {  // past the attended keys: split 0 writes the store only
+      if (split == 0 && warp == 0) {
+        const int pg = slot_new >> 8;
+        fp8_shadow_patch(p, slot_new, kvh, lane, p.k_page_scale ? __ldg(p.k_page_scale + pg * kKvHeads + kvh) : 1.f,
+                         p.v_page_scale ? __ldg(p.v_page_scale + pg * kKvHeads + kvh) : 1.f, 0u, 0);
+      }
+      slot_new = -1;
+    }
+  }
   __syncthreads();
   if (tid == 0 && rg.n_st > 0) {
     tma_prefetch_desc(&p.tm_kc);
@@ -151,6 +193,10 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
     const int valid_end = rg.tok_end;
     const float kscale = meta->kscale[slot], vscale = meta->vscale[slot];
     const int tw0 = t0 + 16 * warp;
+    if (slot_new >= tw0 && slot_new < tw0 + 16) {  // this warp alone reads the slot's row
+      fp8_shadow_patch(p, slot_new, kvh, lane, kscale, vscale, st, slot_new - t0);
+      __syncwarp();
+    }
 
     // ---------------- S^T = K Q^T
     float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};

@@ -433,9 +433,10 @@ int qwz_lse_combine_gathered(const float* gathered, void* out, int32_t world, in
                   "qwz_lse_combine_gathered");
 }
 
-int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const float* k_scale,
-                         const float* v_scale, const int32_t* length, float* part, float* stat,
-                         void* out, int32_t splits, int32_t capacity, void* stream) {
+// Draft split + combine; k_new / v_new / position set: fused shadow write.
+static int fp8_draft(const void* q, const void* k8, const void* v8, const float* k_scale, const float* v_scale,
+                     const int32_t* length, float* part, float* stat, void* out, int32_t splits, int32_t capacity,
+                     void* stream, const void* k_new, const void* v_new, const int32_t* position, const char* what) {
   if (!q || !aligned(q, 16)) return fail(QWZ_EINVAL, "q must be non-null and 16-byte aligned");
   if (!k8 || !v8 || !aligned(k8, 16) || !aligned(v8, 16)) return fail(QWZ_EINVAL, "k8 and v8 must be non-null and 16-byte aligned");
   if (!length || !part || !stat || !out) return fail(QWZ_EINVAL, "length, part, stat and out are required");
@@ -459,16 +460,36 @@ int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const fl
   p.split_len = 0;
   p.num_splits = splits;
   p.sm_scale_log2 = (1.0f / 16.0f) * kLog2e;
+  p.app_k = k_new;
+  p.app_v = v_new;
+  p.app_slot = position;
   // [capacity, 4 x 256 B] views; boxes of 128 head-dim bytes x 128 tokens.
   const uint64_t row_bytes = (uint64_t)qwz::kKvHeads * qwz::kHeadDim;
   int rc = encode_2d(&p.tm_kc, k8, row_bytes, (uint64_t)capacity, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = encode_2d(&p.tm_vc, v8, row_bytes, (uint64_t)capacity, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = launched(qwz::launch_fp8_split(p, as_stream(stream)), "qwz_fp8_draft_decode(split)");
+  rc = launched(qwz::launch_fp8_split(p, as_stream(stream)), what);
   if (rc) return rc;
   const qwz::CombineParams c = split_combine_params(part, stat, qwz::kQHeads, splits, out);
   return launched(qwz::launch_combine(c, qwz::kCombineFinal, QWZ_DTYPE_F16, as_stream(stream)),
-                  "qwz_fp8_draft_decode(combine)");
+                  what);
+}
+
+int qwz_fp8_draft_decode(const void* q, const void* k8, const void* v8, const float* k_scale,
+                         const float* v_scale, const int32_t* length, float* part, float* stat,
+                         void* out, int32_t splits, int32_t capacity, void* stream) {
+  return fp8_draft(q, k8, v8, k_scale, v_scale, length, part, stat, out, splits, capacity, stream, nullptr,
+                   nullptr, nullptr, "qwz_fp8_draft_decode");
+}
+
+int qwz_fp8_draft_step(const void* q, const void* k_new, const void* v_new, const int32_t* position, void* k8,
+                       void* v8, const float* k_scale, const float* v_scale, const int32_t* length, float* part,
+                       float* stat, void* out, int32_t splits, int32_t capacity, void* stream) {
+  if (!k_new || !v_new || !aligned(k_new, 16) || !aligned(v_new, 16))
+    return fail(QWZ_EINVAL, "k_new and v_new must be non-null and 16-byte aligned");
+  if (!position) return fail(QWZ_EINVAL, "position is required");
+  return fp8_draft(q, k8, v8, k_scale, v_scale, length, part, stat, out, splits, capacity, stream, k_new, v_new,
+                   position, "qwz_fp8_draft_step");
 }
 
 int qwz_fp8_shadow_write(const void* k, const void* v, void* k8, void* v8, const float* k_scale,

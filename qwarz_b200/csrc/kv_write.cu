@@ -60,19 +60,9 @@ __global__ void __launch_bounds__(64) fp8_write_kernel(const Fp8WriteParams p) {
   const float* ps = tensor ? p.v_page_scale : p.k_page_scale;
   const float scale = ps ? __ldg(ps + (slot >> 8) * p.num_kv_heads + h) : 1.f;
   const T* src = reinterpret_cast<const T*>(tensor ? p.v : p.k) + (size_t)h * kHeadDim + lane * 8;
-  float x[8];
-  load8<T>(src, x);
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float y = scale == 1.f ? x[j] : __fdiv_rn(x[j], scale);
-    const float c = fminf(fmaxf(y, -448.f), 448.f);
-    const uint32_t b = e4m3_encode_nonneg(fabsf(c)) | (signbit(c) ? 0x80u : 0u);
-    if (j < 4) lo |= b << (8 * j);
-    else hi |= b << (8 * (j - 4));
-  }
+  const uint2 e = fp8_shadow8<T>(src, scale);
   uint8_t* dst = (tensor ? p.v8 : p.k8) + ((size_t)slot * p.num_kv_heads + h) * kHeadDim + lane * 8;
-  *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+  *reinterpret_cast<uint2*>(dst) = e;
 }
 
 // One warp per (batch, token, head); lane handles 8 head-dim elements per

@@ -65,6 +65,25 @@ QWZ_DEVINL void load8(const T* src, float (&x)[8]) {
   }
 }
 
+// FP8 shadow value of 8 consecutive elements (engine/forward/draft.py:
+// 209-210 `_fp8`, with an optional scale): E4M3(clamp(x / scale, +-448)),
+// sign kept, element j in byte j of the little-endian pair.
+template <typename T>
+QWZ_DEVINL uint2 fp8_shadow8(const T* src, float scale) {
+  float x[8];
+  load8<T>(src, x);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float y = scale == 1.f ? x[j] : __fdiv_rn(x[j], scale);
+    const float c = fminf(fmaxf(y, -448.f), 448.f);
+    const uint32_t b = e4m3_encode_nonneg(fabsf(c)) | (signbit(c) ? 0x80u : 0u);
+    if (j < 4) lo |= b << (8 * j);
+    else hi |= b << (8 * (j - 4));
+  }
+  return make_uint2(lo, hi);
+}
+
 // One warp quantises one 256-element row: lane l takes d = 8l..8l+7 (half of
 // block l/2), stores its 4 code bytes, and even lanes store the block scale.
 template <typename T>

@@ -45,6 +45,10 @@ struct alignas(64) SplitParams {
   // Null: no append.
   const void* app_k;
   const void* app_v;
+  // Fused FP8 shadow write (draft step, qwz_fp8_draft_step): app_k / app_v
+  // are FP16 [4, 256] rows for store slot app_slot[0]; the CTA whose stage
+  // holds that slot writes it to the store and into its shared-memory copy.
+  const int32_t* app_slot;
 };
 
 // NVFP4 paged prefill attention (attn_prefill.cu): q [q_len, 24, 256] over

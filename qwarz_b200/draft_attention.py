@@ -64,6 +64,14 @@ class DecodeAttention:
                              self.splits, k_scale, v_scale)
         return out
 
+    def step(self, query, key, value, k_store, v_store, position, length, out, k_scale=None, v_scale=None):
+        """`shadow_write(key, value, ..., position)` then `attend(...)` in two
+        launches: the draft kernel writes the new FP16 rows key, value
+        [.., 4, 256] at slot position[0] of the stores and attends [0, length)."""
+        ops.fp8_draft_step(query, key, value, position, k_store, v_store, length, self.part, self.stat, out,
+                           self.splits, k_scale, v_scale)
+        return out
+
 
 def shadow_write(key, value, k8, v8, position, k_scale=None, v_scale=None):
     """FP8 shadow update at slot position[0]: E4M3(clamp(x / scale, +-448))."""

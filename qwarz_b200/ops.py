@@ -365,6 +365,33 @@ def fp8_draft_decode(q, k8, v8, length, part, stat, out, splits: int, k_scale=No
         splits, cap, _stream(dev)), "qwz_fp8_draft_decode")
 
 
+def fp8_draft_step(q, k_new, v_new, position, k8, v8, length, part, stat, out, splits: int,
+                   k_scale=None, v_scale=None) -> None:
+    """fp8_shadow_write(k_new, v_new, k8, v8, position) then fp8_draft_decode,
+    fused: the draft kernel writes the new FP16 rows [4, 256] at slot
+    position[0] and attends keys [0, length[0])."""
+    dev = _cuda(q, k_new, v_new, position, k8, v8, length, part, stat, out, k_scale, v_scale)
+    if q.dtype != torch.float16 or out.dtype != torch.float16:
+        raise ValueError("draft query and output are float16")
+    for name, t in (("k_new", k_new), ("v_new", v_new)):
+        if t.dtype != torch.float16 or t.numel() != KV_HEADS * DIM:
+            raise ValueError(f"{name} must be one FP16 row [4, 256]")
+        _contig(name, t)
+    for name, t in (("q", q), ("k8", k8), ("v8", v8), ("out", out)):
+        _contig(name, t)
+    for name, t in (("k8", k8), ("v8", v8)):
+        if t.dtype not in (torch.uint8, torch.float8_e4m3fn) or tuple(t.shape[-2:]) != (KV_HEADS, DIM):
+            raise ValueError(f"{name} must be E4M3 [.., T, 4, 256]")
+    cap = k8.numel() // (KV_HEADS * DIM)
+    if part.numel() < HEADS * splits * DIM or stat.numel() < HEADS * splits * 2:
+        raise ValueError("draft workspace too small for splits")
+    _check_page_scales(cap, k_scale, v_scale)
+    lib = _lib.load()
+    _lib.check(lib.qwz_fp8_draft_step(
+        _p(q), _p(k_new), _p(v_new), _p(position), _p(k8), _p(v8), _p(k_scale), _p(v_scale), _p(length),
+        _p(part), _p(stat), _p(out), splits, cap, _stream(dev)), "qwz_fp8_draft_step")
+
+
 def nvfp4_gather(packed, scales, block_table, seq_lens, out, max_tokens: int, page_size: int) -> None:
     """Mirror of the reference `_gather_nvfp4_kernel` launch (xqa.py:73-143)."""
     dev = _cuda(packed, scales, block_table, seq_lens, out)
