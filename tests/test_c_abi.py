@@ -134,3 +134,38 @@ def test_peer_buffer_size_and_exchange_argument_checks(lib):
     assert rc == _lib.QWZ_EINVAL and "16-byte aligned" in msg
     rc, msg = _rc_and_msg(lib, lib.qwz_attn_shard_split(*([addr] * 11), 4, 1, 100, 256, 1, 4, 0.0625, 0, None))
     assert rc == _lib.QWZ_EINVAL and "tok_begin" in msg
+
+
+def test_prefill_draft_prefill_and_draft_step_argument_checks(lib):
+    buf = ctypes.create_string_buffer(4096 + 64)
+    a = (ctypes.addressof(buf) + 63) // 64 * 64
+    # qwz_nvfp4_prefill(q, kc, vc, ks, vs, table, lens, out, table_width, pages, q_len, sm_scale, dtype, stream)
+    for tw, q_len, scale, needle in [(0, 4, 0.0625, "table_width"), (1, 0, 0.0625, "q_len"),
+                                     (1, 4, 0.0, "sm_scale")]:
+        rc, msg = _rc_and_msg(lib, lib.qwz_nvfp4_prefill(*([a] * 8), tw, 1, q_len, scale, 0, None))
+        assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)
+    # qwz_draft_prefill(q, k, v, out, q_len, kv_len, k_stride, v_stride, sm_scale, stream)
+    for args, needle in [((a, None, a, a, 4, 8, 1024, 1024, 0.0625), "k and v"),
+                         ((a, a, a, a, 9, 8, 1024, 1024, 0.0625), "q_len <= kv_len"),
+                         ((a, a, a, a, 4, 8, 1000, 1024, 0.0625), "token strides"),
+                         ((a, a, a, a, 4, 8, 1024, 1028, 0.0625), "token strides"),
+                         ((a, a, a, a, 4, 8, 1024, 1024, -1.0), "sm_scale")]:
+        rc, msg = _rc_and_msg(lib, lib.qwz_draft_prefill(*args, None))
+        assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)
+    # qwz_fp8_draft_step(q, k_new, v_new, position, k8, v8, ks, vs, length, part, stat, out, splits, cap, stream)
+    rc, msg = _rc_and_msg(lib, lib.qwz_fp8_draft_step(a, None, a, a, a, a, None, None, a, a, a, a, 4, 256, None))
+    assert rc == _lib.QWZ_EINVAL and "k_new" in msg
+    rc, msg = _rc_and_msg(lib, lib.qwz_fp8_draft_step(a, a, a, None, a, a, None, None, a, a, a, a, 4, 256, None))
+    assert rc == _lib.QWZ_EINVAL and "position" in msg
+    rc, msg = _rc_and_msg(lib, lib.qwz_fp8_draft_step(a, a, a, a, a, a, None, None, a, a, a, a, 0, 256, None))
+    assert rc == _lib.QWZ_EINVAL and "splits" in msg
+
+
+def test_draft_prefill_ops_refuse_cpu_and_non_fp16():
+    import torch
+    from qwarz_b200 import ops
+
+    q = torch.zeros(1, 8, 24, 256, dtype=torch.float16)
+    kv = torch.zeros(1, 16, 4, 256, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.draft_prefill(q, kv, kv, torch.empty_like(q))
