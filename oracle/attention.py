@@ -30,8 +30,8 @@ def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sm_scale: 
     kf = k.float().permute(1, 0, 2)
     vf = v.float().permute(1, 0, 2)
     scores = torch.bmm(qg, kf.transpose(1, 2)) * sm_scale  # [4, 6S, L]
-    s_idx = torch.arange(GROUP * S) % S
-    visible = torch.arange(L)[None, :] <= (pre_len + s_idx)[:, None]
+    s_idx = torch.arange(GROUP * S, device=q.device) % S
+    visible = torch.arange(L, device=q.device)[None, :] <= (pre_len + s_idx)[:, None]
     scores = scores.masked_fill(~visible[None], float("-inf"))
     probs = torch.softmax(scores, dim=-1)
     out = torch.bmm(probs, vf)  # [4, 6S, D]

@@ -169,18 +169,28 @@ _E4M3_T = torch.from_numpy(e4m3_decode(np.arange(256, dtype=np.uint8)))
 
 
 def dequant_rows_torch(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
-    """float32 dequant of CPU uint8 tensors (same arithmetic as dequant_rows)."""
+    """float32 dequant of uint8 tensors (same arithmetic as dequant_rows).
+    The lookup tables follow the operands' device, so the checker can run
+    beside the kernels at full size; the arithmetic is one exact product."""
+    e2m1 = _E2M1_T.to(packed.device)
+    e4m3 = _E4M3_T.to(packed.device)
     lo = (packed & 0xF).long()
     hi = (packed >> 4).long()
-    vals = torch.stack([_E2M1_T[lo], _E2M1_T[hi]], dim=-1).flatten(-2)
-    sc = _E4M3_T[scales.long()].repeat_interleave(16, dim=-1)
+    vals = torch.stack([e2m1[lo], e2m1[hi]], dim=-1).flatten(-2)
+    sc = e4m3[scales.view(torch.uint8).long()].repeat_interleave(16, dim=-1)
     return vals * sc
+
+
+def e4m3_decode_torch(b: torch.Tensor) -> torch.Tensor:
+    """float32 values of E4M3 bytes (uint8 or float8_e4m3fn), by table lookup."""
+    return _E4M3_T.to(b.device)[b.view(torch.uint8).long()]
 
 
 def gather_logical_torch(packed: torch.Tensor, scales: torch.Tensor, block_table: torch.Tensor,
                          length: int, page: int = 256, chunk_pages: int = 64) -> torch.Tensor:
     """float32 [length, heads, dim] of the first `length` logical tokens."""
     n_pages = (length + page - 1) // page
+    scales = scales.view(torch.uint8)
     parts = []
     for p0 in range(0, n_pages, chunk_pages):
         ids = block_table[p0:min(n_pages, p0 + chunk_pages)].long()
