@@ -7,13 +7,16 @@ Default workload ("auto"): one decode step = q_len 1 attention over 16
 attention layers, each with independent seeded NVFP4 KV of 65,536 tokens per
 GPU (BASELINE config 2 at N=1).  At N > 1 the 16 sequences are 65,536*N
 tokens long and sharded contiguously by pages (N=4 is the 262,144-token
-native context of config 4): per layer every rank appends (the owner
-writes), computes its shard's (m, l, O) record, all-gathers the records over
-NCCL and LSE-combines them — "scaling": "weak" (per-GPU work fixed).
+native context of config 4): per layer every rank runs the shard split (the
+owner of the new row's page appends it), then one kernel merges its splits
+into an (m, l, O) record, stores it into every rank's buffer over NVLink peer
+memory and LSE-combines all records (--exchange nccl: an NCCL all-gather and
+a separate combine) — "scaling": "weak" (per-GPU work fixed).
 
 value  = whole-job algorithmic HBM bytes per step / device step time (GB/s);
          per layer 1152*L + 2*(24*256*2) + 4*P + 1152 + 2*4*256*2 bytes.
-e2e    = the same bytes through the public API `qwarz_b200.attention.attend`
+e2e    = the same bytes through the C-ABI call a caller makes per layer
+         (qwz_nvfp4_attend via qwarz_b200.ops; ShardedDecode.step at N > 1),
          with every step's Q/K/V copied in from pinned host memory and the
          outputs copied back, all inside the timed region.
 roofline: the split kernel alone (graph of its 16 launches), CUDA events.
