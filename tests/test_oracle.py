@@ -123,6 +123,22 @@ def test_dequant_torch_equals_numpy():
     a = nvfp4.dequant_rows(c["k_cache"], c["k_scales"])
     b = nvfp4.dequant_rows_torch(torch.from_numpy(c["k_cache"]), torch.from_numpy(c["k_scales"])).numpy()
     np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    # scales given as float8_e4m3fn (the cache's own dtype) read the same bytes
+    f8 = torch.from_numpy(c["k_scales"]).view(torch.float8_e4m3fn)
+    b8 = nvfp4.dequant_rows_torch(torch.from_numpy(c["k_cache"]), f8).numpy()
+    np.testing.assert_array_equal(a.view(np.uint32), b8.view(np.uint32))
+
+
+def test_e4m3_decode_torch_equals_numpy_on_every_byte():
+    allb = np.arange(256, dtype=np.uint8)
+    want = nvfp4.e4m3_decode(allb)
+    for t in (torch.from_numpy(allb), torch.from_numpy(allb).view(torch.float8_e4m3fn)):
+        got = nvfp4.e4m3_decode_torch(t).numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    # and torch's own float8 cast agrees on every non-NaN byte
+    ref = torch.from_numpy(allb).view(torch.float8_e4m3fn).float().numpy()
+    finite = ~np.isnan(want)
+    np.testing.assert_array_equal(ref[finite], want[finite])
 
 
 # ---------------------------------------------------------- attention math
