@@ -196,3 +196,20 @@ def test_gloo_rank_failure_surfaces_as_error_on_peers():
     res = _run(2, 1000, fail_rank=1)
     assert res[1][0] == "error" and "injected" in res[1][1]
     assert res[0][0] == "error", res[0]    # the peer's collective fails (timeout/abort), no hang
+
+
+def test_bench_algorithmic_bytes_per_layer_call():
+    """The roofline's algorithmic bytes: 1,152 B per cached token (codes and
+    scales of K and V), Q in and O out, the table, the appended rows and the
+    new K/V read, at the BASELINE configs."""
+    import bench
+
+    def expect(L, q_len):
+        pages = math.ceil(L / 256)
+        return 1152 * L + 2 * (q_len * 24 * 256 * 2) + 4 * pages + 1152 * q_len + 2 * q_len * 4 * 256 * 2
+
+    for L, q_len, mb in ((4096, 1, 4.75), (65536, 1, 75.53), (32768, 7, 37.96), (131072, 7, 151.21),
+                         (262144, 1, 302.02)):
+        got = bench.layer_bytes(L, q_len)
+        assert got == expect(L, q_len)
+        assert abs(got / 1e6 - mb) < 0.01, (L, q_len, got)
