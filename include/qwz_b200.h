@@ -119,6 +119,39 @@ int qwz_attn_combine(const float* partial_o, const float* partial_ml, void* out,
                      int32_t dtype, void* stream);
 
 /*
+ * Graph patching of captured split / combine launches.  The reference's
+ * decode graphs patch split arguments 3, 4, 11, 12, 13 (block_table,
+ * cache_seqlens, split_len, num_pages_per_seq, num_splits) and combine
+ * argument 4 (num_splits) between replays
+ * (docs/superpowers/specs/2026-09-11-qwasar-attention-kernel.md:66-74,
+ * tests/test_attention_kernel_abi.py:25-31).  Here a captured split or
+ * combine launch (from qwz_attn_split, qwz_attn_combine or
+ * qwz_nvfp4_attend) is one kernel node whose single parameter packs those
+ * arguments:
+ *   qwz_graph_kernel_nodes  lists the split (QWZ_NODE_SPLIT) or combine
+ *                           (QWZ_NODE_COMBINE) nodes of this library in a
+ *                           cudaGraph_t, in the graph's node order: up to
+ *                           max_nodes handles into nodes, the total in count;
+ *   qwz_graph_patch_split   sets the five split arguments of one node, in the
+ *                           graph and, if graph_exec is not NULL, in that
+ *                           instantiated graph (the split grid follows
+ *                           num_splits);
+ *   qwz_graph_patch_combine sets num_splits of one combine node that reads
+ *                           the split ABI's partial layout.
+ * The workspace (partial_o, partial_ml) must hold the new num_splits, and
+ * the new block_table / cache_seqlens must stay valid for every later
+ * replay.  The pool (k/v caches and scales) cannot be patched.  Do not patch
+ * a graph_exec while it is being replayed.
+ */
+#define QWZ_NODE_SPLIT 0
+#define QWZ_NODE_COMBINE 1
+int qwz_graph_kernel_nodes(void* graph, int32_t kind, void** nodes, int32_t max_nodes, int32_t* count);
+int qwz_graph_patch_split(void* graph, void* graph_exec, void* node, const int32_t* block_table,
+                          const int32_t* cache_seqlens, int32_t split_len, int32_t num_pages_per_seq,
+                          int32_t num_splits);
+int qwz_graph_patch_combine(void* graph, void* graph_exec, void* node, int32_t num_splits);
+
+/*
  * The adapter's decode/verify route in one call: append + split + combine
  * (replaces NVFP4AttentionAdapter._append + _xqa, src/qwasar_runtime/
  * xqa.py:356-379 and 484-554).  k, v: the q_len new rows [q_len, 4, 256];
@@ -168,7 +201,9 @@ int qwz_draft_prefill(const void* q, const void* k, const void* v, void* out, in
  * held by every GPU that loads the library until the process exits.
  * Requests with q_len * 24 * num_splits > 4096 return QWZ_EINVAL.  The first
  * call on a device resolves the array's device address (cudaGetSymbolAddress
- * with that device current) and must come before any stream capture on it.
+ * with that device current) and must come before any stream capture on it;
+ * after a cudaDeviceReset the next call resolves it again (likewise outside
+ * a capture).
  * Calls share the array and race if they overlap on the GPU: serialise them.
  * Allocates nothing; arguments otherwise as qwz_nvfp4_attend.
  */
@@ -233,18 +268,25 @@ int qwz_attn_shard_split(const void* q, const void* k, const void* v, void* k_ca
 
 /*
  * Exchange and merge in one kernel: merges this rank's num_splits partials
- * into one (m, l, O) record per query row, stores it into every rank's
- * buffer, raises the row's flag there and, once every rank's record is in
- * (bounded wait; a timeout sets QWZ_DEVERR_TIMEOUT), LSE-merges them in rank
- * order into out [q_len, 24, 256] FP16/BF16 (the same on every rank).
- *   peers   HOST array [world] of the buffers' device addresses as this GPU
- *           maps them (its own buffer at [rank])
- *   epochs  device uint32 [q_len * 24], zeroed once; the kernel counts calls
+ * into one (m, l, O) record per query row and stores it into every rank's
+ * buffer, each value in a 64-bit word tagged with the epoch of this call (no
+ * separate flag: a reader polls the data words until they carry the epoch
+ * it waits for).  Once every rank's record is in its own buffer it
+ * LSE-merges them in rank order into out [q_len, 24, 256] FP16/BF16 (the
+ * same on every rank).  The wait is bounded: after timeout_ns (0: 0.5 s) the
+ * kernel sets QWZ_DEVERR_TIMEOUT, merges what has arrived and returns.
+ *   peers        HOST array [world] of the buffers' device addresses as this
+ *                GPU maps them (its own buffer at [rank])
+ *   buffer_bytes the size the buffers were allocated with; must equal
+ *                qwz_peer_buffer_bytes(world, q_len) (QWZ_EINVAL otherwise)
+ *   epochs       device uint32 [q_len * 24], zeroed once; the kernel counts
+ *                calls
  * Every rank must call it the same number of times, with the same q_len.
  */
 int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, int32_t num_splits,
-                               int32_t q_len, const uint64_t* peers, uint32_t* epochs, int32_t rank,
-                               int32_t world, void* out, int32_t dtype, void* stream);
+                               int32_t q_len, const uint64_t* peers, int64_t buffer_bytes, uint32_t* epochs,
+                               int32_t rank, int32_t world, void* out, int64_t timeout_ns, int32_t dtype,
+                               void* stream);
 
 /*
  * The same for `world` ranks emulated on one GPU in one cooperative launch
@@ -255,8 +297,9 @@ int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, 
  */
 int qwz_shard_exchange_combine_emulated(const float* partial_o, const float* partial_ml,
                                         int64_t rank_stride_splits, int32_t num_splits, int32_t q_len,
-                                        const uint64_t* peers, uint32_t* epochs, void* out,
-                                        int32_t world, int32_t dtype, void* stream);
+                                        const uint64_t* peers, int64_t buffer_bytes, uint32_t* epochs,
+                                        void* out, int32_t world, int64_t timeout_ns, int32_t dtype,
+                                        void* stream);
 
 /*
  * FP8 shadow-KV draft decode (replaces DecodeAttention.attend,

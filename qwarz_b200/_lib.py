@@ -17,6 +17,8 @@ QWZ_EINVAL = -1
 QWZ_ELAUNCH = -2
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
+NODE_SPLIT = 0
+NODE_COMBINE = 1
 
 _i32p = POINTER(c_int32)
 _f32p = POINTER(c_float)
@@ -46,10 +48,14 @@ SIGNATURES = {
     "qwz_peer_close": [c_void_p],
     "qwz_peer_free": [c_void_p],
     "qwz_attn_shard_split": [c_void_p] * 11 + [c_int32] * 6 + [c_float, c_int32, c_void_p],
-    "qwz_shard_exchange_combine": [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p,
-                                   c_int32, c_int32, c_void_p, c_int32, c_void_p],
+    "qwz_shard_exchange_combine": [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int64, c_void_p,
+                                   c_int32, c_int32, c_void_p, c_int64, c_int32, c_void_p],
+    "qwz_graph_kernel_nodes": [c_void_p, c_int32, c_void_p, c_int32, _i32p],
+    "qwz_graph_patch_split": [c_void_p] * 5 + [c_int32] * 3,
+    "qwz_graph_patch_combine": [c_void_p] * 3 + [c_int32],
     "qwz_shard_exchange_combine_emulated": [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p,
-                                            c_void_p, c_void_p, c_int32, c_int32, c_void_p],
+                                            c_int64, c_void_p, c_void_p, c_int32, c_int64, c_int32,
+                                            c_void_p],
 }
 _RESTYPE = {"qwz_version": c_char_p, "qwz_last_error": c_char_p, "qwz_peer_buffer_bytes": c_int64}
 

@@ -8,6 +8,8 @@ argument 4 (num_splits) is int32.
 """
 from __future__ import annotations
 
+import ctypes
+
 from .. import _lib
 
 SPLIT_ARG_NAMES = (
@@ -67,3 +69,34 @@ def call_combine(partial_o: int, partial_ml: int, out: int, num_splits: int, q_l
     lib = _lib.load()
     _lib.check(lib.qwz_attn_combine(partial_o, partial_ml, out, None, num_splits, None, q_len,
                                     dtype, stream), "qwz_attn_combine")
+
+
+# ------------------------------------------------------------ graph patching
+def graph_nodes(graph: int, kind: int) -> list[int]:
+    """This library's split (kind 0) or combine (kind 1) kernel nodes of a
+    cudaGraph_t (an int handle, e.g. torch's CUDAGraph(keep_graph=True)
+    .raw_cuda_graph()), in the graph's node order."""
+    lib = _lib.load()
+    count = ctypes.c_int32(0)
+    _lib.check(lib.qwz_graph_kernel_nodes(graph, kind, None, 0, ctypes.byref(count)), "qwz_graph_kernel_nodes")
+    nodes = (ctypes.c_void_p * max(count.value, 1))()
+    _lib.check(lib.qwz_graph_kernel_nodes(graph, kind, nodes, count.value, ctypes.byref(count)),
+               "qwz_graph_kernel_nodes")
+    return [int(nodes[i]) for i in range(count.value)]
+
+
+def patch_split(graph: int, graph_exec: int | None, node: int, packed) -> None:
+    """Patch the graph-patch indices of one captured split node (3, 4, 11,
+    12, 13: block_table, cache_seqlens, split_len, num_pages_per_seq,
+    num_splits) from a `pack_split_args` list."""
+    values = {name: value for name, _, value in packed}
+    lib = _lib.load()
+    _lib.check(lib.qwz_graph_patch_split(graph, graph_exec, node, values["block_table"], values["cache_seqlens"],
+                                         values["split_len"], values["num_pages_per_seq"], values["num_splits"]),
+               "qwz_graph_patch_split")
+
+
+def patch_combine(graph: int, graph_exec: int | None, node: int, num_splits: int) -> None:
+    """Patch combine argument 4 (num_splits) of one captured combine node."""
+    lib = _lib.load()
+    _lib.check(lib.qwz_graph_patch_combine(graph, graph_exec, node, num_splits), "qwz_graph_patch_combine")

@@ -47,13 +47,18 @@ def build_contract() -> dict:
             },
         },
         "geometry": {
-            # the reference's donor Attention64 row layout for q_len 7 (the
-            # kernel this library replaces, tests/test_attention_kernel_abi.py:51-55)
+            # the reference's donor Attention64 row layout for q_len 7, which
+            # its ABI test pins (tests/test_attention_kernel_abi.py:51-55); it
+            # describes the kernel this library replaces, not one it runs
             "q7_layout": {"BLOCK_M": 8, "BLOCK_H": 2, "BLOCK_ROWS": 16, "programs": 12, "BLOCK_N": 64},
+            "q7_layout_scope": "donor Attention64 (replaced); the sm_100a kernels' layout is geometry.b200",
             "b200": {
-                "q1": {"mma_m": "16 tokens", "mma_n": "8 (6 GQA heads + 2 pad)", "stage_tokens": 64},
-                "q7": {"rows": 42, "mma_n": "48 (6 n-tiles)", "stage_tokens": 64,
-                       "phase1": "token split", "phase2": "head-dim split"},
+                "q1": {"kernel": "nvfp4_decode_kernel", "stage_tokens": 256, "stages": 3,
+                       "mma": "mma.sync m16n8k16", "mma_m": "16 tokens", "mma_n": "8 (6 GQA heads + 2 pad)",
+                       "tokens_per_warp_per_stage": 32},
+                "q7": {"kernel": "nvfp4_verify_tc_kernel", "rows": 42, "stage_tokens": 128,
+                       "mma": "tcgen05 kind::f16", "qk": "S^T[128 tokens x 48] = K Q^T, K in tensor memory",
+                       "pv": "O^T[256 d x 48] += V^T P^T, two M=128 halves of d, V and P in shared memory"},
             },
         },
         "decode_policy": backend.DECODE_POLICY,

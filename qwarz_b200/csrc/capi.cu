@@ -612,13 +612,23 @@ int qwz_attn_shard_split(const void* q, const void* k, const void* v, void* k_ca
 }
 
 namespace {
+constexpr int64_t kExchangeTimeoutDefaultNs = 500ll * 1000 * 1000;  // 0.5 s
+constexpr int64_t kExchangeTimeoutMaxNs = 10ll * 1000 * 1000 * 1000;  // 10 s
+
 int fill_exchange(qwz::ExchangeParams& x, int32_t num_splits, int32_t q_len, const uint64_t* peers,
-                  int32_t world) {
+                  int64_t buffer_bytes, int32_t world, int64_t timeout_ns) {
   if (world < 1 || world > qwz::kMaxWorld) return fail(QWZ_EINVAL, "world must be in 1..8");
   if (q_len < 1 || q_len > 8) return fail(QWZ_EINVAL, "q_len must be in 1..8");
   if (num_splits < 1 || num_splits > 65535) return fail(QWZ_EINVAL, "num_splits must be in 1..65535");
   if (!peers) return fail(QWZ_EINVAL, "peers (host array of buffer addresses) is required");
+  // the buffers are laid out for one (world, q_len): any other pair would
+  // store past their end or read a stale record of the same epoch
+  if (buffer_bytes != qwz_peer_buffer_bytes(world, q_len))
+    return fail(QWZ_EINVAL, "buffer_bytes must be qwz_peer_buffer_bytes(world, q_len) of the buffers' allocation");
+  if (timeout_ns < 0 || timeout_ns > kExchangeTimeoutMaxNs)
+    return fail(QWZ_EINVAL, "timeout_ns must be in 0..1e10 (0: the default 0.5 s)");
   x = qwz::ExchangeParams{};
+  x.timeout_ns = (unsigned long long)(timeout_ns == 0 ? kExchangeTimeoutDefaultNs : timeout_ns);
   for (int g = 0; g < world; ++g) {
     if (!peers[g] || peers[g] % 16) return fail(QWZ_EINVAL, "every peer buffer address must be non-null and 16-byte aligned");
     x.peers[g] = peers[g];
@@ -631,13 +641,14 @@ int fill_exchange(qwz::ExchangeParams& x, int32_t num_splits, int32_t q_len, con
 }  // namespace
 
 int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, int32_t num_splits,
-                               int32_t q_len, const uint64_t* peers, uint32_t* epochs, int32_t rank,
-                               int32_t world, void* out, int32_t dtype, void* stream) {
+                               int32_t q_len, const uint64_t* peers, int64_t buffer_bytes, uint32_t* epochs,
+                               int32_t rank, int32_t world, void* out, int64_t timeout_ns, int32_t dtype,
+                               void* stream) {
   int rc = check_dtype(dtype);
   if (rc) return rc;
   if (!partial_o || !partial_ml || !epochs || !out) return fail(QWZ_EINVAL, "partials, epochs and out are required");
   qwz::ExchangeParams x;
-  rc = fill_exchange(x, num_splits, q_len, peers, world);
+  rc = fill_exchange(x, num_splits, q_len, peers, buffer_bytes, world, timeout_ns);
   if (rc) return rc;
   if (rank < 0 || rank >= world) return fail(QWZ_EINVAL, "rank must be in 0..world-1");
   x.po[0] = partial_o;
@@ -650,13 +661,14 @@ int qwz_shard_exchange_combine(const float* partial_o, const float* partial_ml, 
 
 int qwz_shard_exchange_combine_emulated(const float* partial_o, const float* partial_ml,
                                         int64_t rank_stride_splits, int32_t num_splits, int32_t q_len,
-                                        const uint64_t* peers, uint32_t* epochs, void* out,
-                                        int32_t world, int32_t dtype, void* stream) {
+                                        const uint64_t* peers, int64_t buffer_bytes, uint32_t* epochs,
+                                        void* out, int32_t world, int64_t timeout_ns, int32_t dtype,
+                                        void* stream) {
   int rc = check_dtype(dtype);
   if (rc) return rc;
   if (!partial_o || !partial_ml || !epochs || !out) return fail(QWZ_EINVAL, "partials, epochs and out are required");
   qwz::ExchangeParams x;
-  rc = fill_exchange(x, num_splits, q_len, peers, world);
+  rc = fill_exchange(x, num_splits, q_len, peers, buffer_bytes, world, timeout_ns);
   if (rc) return rc;
   if (rank_stride_splits < num_splits) return fail(QWZ_EINVAL, "rank_stride_splits must be >= num_splits");
   const int64_t rows = (int64_t)q_len * qwz::kQHeads;

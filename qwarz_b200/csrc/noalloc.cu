@@ -15,8 +15,9 @@
 //   - host code cannot pass the array's name to a kernel (on the host it is a
 //     stand-in, not a device address): the first call on each device resolves
 //     the device address with cudaGetSymbolAddress, with that device current,
-//     and caches it, so that first call should be made before any stream
-//     capture;
+//     and caches it with the device's context, so that first call should be
+//     made before any stream capture (after a cudaDeviceReset the next call
+//     resolves it again, and that call too belongs outside a capture);
 //   - all calls share the array and it keeps the last call's contents; the
 //     split kernel rewrites every record it owns (empty splits write
 //     m = -inf), so nothing needs clearing, but calls that overlap on the GPU
@@ -40,11 +41,33 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 
-// Device address of g_noalloc_scratch on the current device (resolved once
-// per device), or nullptr with *err set.
+// The CUDA context current on this thread (through the runtime's driver
+// entry point; the library links only the static runtime), or nullptr.
+CUcontext current_context() {
+  using Fn = CUresult (*)(CUcontext*);
+  static Fn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<Fn>(f);
+  });
+  CUcontext ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+// Device address of g_noalloc_scratch on the current device, or nullptr
+// with *err set.  Resolved once per device and context: the first call on a
+// device looks it up with that device current, and a later call does so
+// again only if the device's context has changed since (after
+// cudaDeviceReset the module is loaded anew and the array may move).
 float* noalloc_scratch(cudaError_t* err) {
   static std::mutex mu;
   static float* addr[kMaxDevices] = {};
+  static CUcontext owner[kMaxDevices] = {};
   int dev = -1;
   *err = cudaGetDevice(&dev);
   if (*err != cudaSuccess) return nullptr;
@@ -53,11 +76,14 @@ float* noalloc_scratch(cudaError_t* err) {
     return nullptr;
   }
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  const CUcontext ctx = current_context();
+  if (addr[dev] == nullptr || ctx != owner[dev]) {
     void* p = nullptr;
     *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (*err != cudaSuccess) return nullptr;
     addr[dev] = static_cast<float*>(p);
+    // the symbol lookup makes the runtime's context current if none was
+    owner[dev] = ctx != nullptr ? ctx : current_context();
   }
   return addr[dev];
 }

@@ -10,3 +10,4 @@
 #include "kv_write.cu"
 #include "capi.cu"
 #include "noalloc.cu"
+#include "graph_patch.cu"

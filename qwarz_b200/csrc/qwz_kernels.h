@@ -134,6 +134,7 @@ struct ExchangeParams {
   int rows;
   int world;
   int rank0;
+  unsigned long long timeout_ns; // bound of each rank's wait for the others' records
 };
 
 cudaError_t launch_nvfp4_split(const SplitParams& p, int dtype, cudaStream_t stream);

@@ -18,9 +18,10 @@
 //   2. stores it, tagged with e = this row's call count, into every rank's
 //      buffer at [g][r] (stores into the peers' memory);
 //   3. reads the world records of row r from its own buffer, waiting per
-//      word until it carries epoch e (bounded by globaltimer: a timeout sets
-//      kErrTimeout and merges what is there), and merges them in rank order,
-//      so every rank writes the same output.
+//      word until it carries epoch e (bounded by globaltimer, p.timeout_ns
+//      for the whole row: a timeout sets kErrTimeout and merges what is
+//      there), and merges them in rank order, so every rank writes the same
+//      output.
 // Epochs count calls per row on every rank (a device word per row, advanced
 // by the kernel), so repeated launches and CUDA-graph replays need no reset.
 // With fewer GPUs than ranks the kernel runs all ranks in one cooperative
@@ -36,7 +37,6 @@ namespace qwz {
 
 namespace {
 
-constexpr uint64_t kExchangeTimeoutNs = 500ull * 1000 * 1000;  // 0.5 s
 constexpr int kRecWords = kHeadDim + 2;                         // m, l, O[256]
 
 QWZ_DEVINL uint64_t global_ns() {
@@ -53,8 +53,9 @@ QWZ_DEVINL uint64_t ld_tagged(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
-// The value of a tagged word once it carries epoch e; false on timeout.
-QWZ_DEVINL bool wait_tagged(const uint64_t* p, uint32_t e, uint64_t t0, float& v) {
+// The value of a tagged word once it carries epoch e; false once
+// timeout_ns have passed since t0.
+QWZ_DEVINL bool wait_tagged(const uint64_t* p, uint32_t e, uint64_t t0, uint64_t timeout_ns, float& v) {
   for (int i = 0;; ++i) {
     const uint64_t w = ld_tagged(p);
     if ((uint32_t)(w >> 32) == e) {
@@ -62,7 +63,7 @@ QWZ_DEVINL bool wait_tagged(const uint64_t* p, uint32_t e, uint64_t t0, float& v
       return true;
     }
     if ((i & 63) == 63) {
-      if (global_ns() - t0 > kExchangeTimeoutNs) {
+      if (global_ns() - t0 > timeout_ns) {
         v = __uint_as_float((uint32_t)w);
         return false;
       }
@@ -185,9 +186,9 @@ __global__ void __launch_bounds__(256) shard_exchange_kernel(const ExchangeParam
     lg[g] = og[g] = 0.f;
     if (g < p.world) {
       const uint64_t* src = local + half + ((size_t)g * rows + r) * kRecWords;
-      ok &= wait_tagged(src, e, t0, mg[g]);
-      ok &= wait_tagged(src + 1, e, t0, lg[g]);
-      ok &= wait_tagged(src + 2 + tid, e, t0, og[g]);
+      ok &= wait_tagged(src, e, t0, p.timeout_ns, mg[g]);
+      ok &= wait_tagged(src + 1, e, t0, p.timeout_ns, lg[g]);
+      ok &= wait_tagged(src + 2 + tid, e, t0, p.timeout_ns, og[g]);
     }
   }
   if (!ok) flag_error(kErrTimeout);

@@ -308,33 +308,38 @@ def shard_split(q, k, v, k_cache, v_cache, k_scales, v_scales, block_table, cach
         q_len, num_splits, float(sm_scale), _dtype_code(q.dtype), _stream(dev)), "qwz_attn_shard_split")
 
 
-def shard_exchange_combine(partial_o, partial_ml, num_splits: int, peers, epochs, rank: int, world: int,
-                           out) -> None:
+def shard_exchange_combine(partial_o, partial_ml, num_splits: int, peers, buffer_bytes: int, epochs,
+                           rank: int, world: int, out, timeout_ns: int = 0) -> None:
     """Merge this rank's splits, exchange the records over peer memory and merge
     all ranks' records into out; `peers` is a ctypes uint64 array of the
-    ranks' exchange buffers as this GPU maps them."""
+    ranks' exchange buffers as this GPU maps them, `buffer_bytes` the size
+    they were allocated with.  The wait for the other ranks gives up after
+    timeout_ns (0: 0.5 s) and sets QWZ_DEVERR_TIMEOUT."""
     dev = _cuda(partial_o, partial_ml, epochs, out)
     q_len = out.numel() // (HEADS * DIM)
     if epochs.dtype != torch.int32 or epochs.numel() < q_len * HEADS:
         raise ValueError("epochs must be int32 with q_len*24 elements")
     lib = _lib.load()
     _lib.check(lib.qwz_shard_exchange_combine(
-        _p(partial_o), _p(partial_ml), num_splits, q_len, ctypes.cast(peers, ctypes.c_void_p), _p(epochs),
-        rank, world, _p(out), _dtype_code(out.dtype), _stream(dev)), "qwz_shard_exchange_combine")
+        _p(partial_o), _p(partial_ml), num_splits, q_len, ctypes.cast(peers, ctypes.c_void_p), int(buffer_bytes),
+        _p(epochs), rank, world, _p(out), int(timeout_ns), _dtype_code(out.dtype), _stream(dev)),
+        "qwz_shard_exchange_combine")
 
 
-def shard_exchange_combine_emulated(partial_o, partial_ml, num_splits: int, peers, epochs, out) -> None:
+def shard_exchange_combine_emulated(partial_o, partial_ml, num_splits: int, peers, buffer_bytes: int, epochs,
+                                    out, timeout_ns: int = 0) -> None:
     """All ranks on one GPU (one cooperative launch): partial_o [world, rows,
     splits, 256], partial_ml [world, rows, splits, 2], epochs int32
-    [world, rows], out [world, rows, 256]; peers[g] = rank g's buffer."""
+    [world, rows], out [world, rows, 256]; peers[g] = rank g's buffer, each
+    of buffer_bytes."""
     dev = _cuda(partial_o, partial_ml, epochs, out)
     world = partial_o.shape[0]
     q_len = out[0].numel() // (HEADS * DIM)
     lib = _lib.load()
     _lib.check(lib.qwz_shard_exchange_combine_emulated(
         _p(partial_o), _p(partial_ml), partial_o.shape[2], num_splits, q_len,
-        ctypes.cast(peers, ctypes.c_void_p), _p(epochs), _p(out), world, _dtype_code(out.dtype),
-        _stream(dev)), "qwz_shard_exchange_combine_emulated")
+        ctypes.cast(peers, ctypes.c_void_p), int(buffer_bytes), _p(epochs), _p(out), world, int(timeout_ns),
+        _dtype_code(out.dtype), _stream(dev)), "qwz_shard_exchange_combine_emulated")
 
 
 def combine_gathered(gathered, out, world: int) -> None:

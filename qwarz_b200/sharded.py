@@ -95,6 +95,7 @@ class PeerExchange:
         nbytes = lib.qwz_peer_buffer_bytes(world, q_len)
         if nbytes <= 0:
             raise ValueError("world must be 1..8 and q_len 1..8")
+        self.nbytes = nbytes
         own = ctypes.c_void_p()
         handle = (ctypes.c_uint8 * 64)()
         with torch.cuda.device(self.device):
@@ -141,8 +142,9 @@ class ShardedDecode:
     peer-memory exchange kernel)."""
 
     def __init__(self, shard: Shard, device, q_len: int = 1, num_splits: int | None = None,
-                 group=None, exchange: str = "auto"):
+                 group=None, exchange: str = "auto", timeout_ns: int = 0):
         self.shard = shard
+        self.timeout_ns = timeout_ns  # bound of the peer exchange's wait (0: 0.5 s)
         self.device = torch.device(device)
         self.q_len = q_len
         self.group = group
@@ -184,7 +186,8 @@ class ShardedDecode:
                             self.partial_o, self.partial_ml, self.shard.tok_begin, self.shard.tok_span,
                             self.splits, sm_scale)
             ops.shard_exchange_combine(self.partial_o, self.partial_ml, self.splits, self.peer.peers,
-                                       self.peer.epochs, self.shard.rank, self.shard.world, out)
+                                       self.peer.nbytes, self.peer.epochs, self.shard.rank, self.shard.world,
+                                       out, self.timeout_ns)
             return out
         self.append(k, v, cache, local_table, cache_seqlens)
         self.partial(q, cache, local_table, cache_seqlens, sm_scale)

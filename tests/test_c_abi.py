@@ -122,16 +122,24 @@ def test_peer_buffer_size_and_exchange_argument_checks(lib):
     addr = (ctypes.addressof(buf) + 63) // 64 * 64
     peers = (ctypes.c_uint64 * 2)(addr, addr)
     pv = ctypes.cast(peers, ctypes.c_void_p)
-    for world, rank, q_len, splits, p, needle in [
-            (9, 0, 1, 4, pv, "world"), (2, 2, 1, 4, pv, "rank"), (2, 0, 0, 4, pv, "q_len"),
-            (2, 0, 1, 0, pv, "num_splits"), (2, 0, 1, 4, None, "peers")]:
-        rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine(addr, addr, splits, q_len, p, addr, rank,
-                                                                  world, addr, 0, None))
+    nb = lib.qwz_peer_buffer_bytes(2, 1)
+    for world, rank, q_len, splits, p, nbytes, timeout, needle in [
+            (9, 0, 1, 4, pv, nb, 0, "world"), (2, 2, 1, 4, pv, nb, 0, "rank"), (2, 0, 0, 4, pv, nb, 0, "q_len"),
+            (2, 0, 1, 0, pv, nb, 0, "num_splits"), (2, 0, 1, 4, None, nb, 0, "peers"),
+            # buffers sized for another (world, q_len): refused before any store
+            (2, 0, 2, 4, pv, nb, 0, "buffer_bytes"), (4, 0, 1, 4, pv, nb, 0, "buffer_bytes"),
+            (2, 0, 1, 4, pv, nb + 8, 0, "buffer_bytes"),
+            (2, 0, 1, 4, pv, nb, -1, "timeout_ns"), (2, 0, 1, 4, pv, nb, 10**10 + 1, "timeout_ns")]:
+        rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine(addr, addr, splits, q_len, p, nbytes, addr, rank,
+                                                                  world, addr, timeout, 0, None))
         assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)
     bad = (ctypes.c_uint64 * 2)(addr + 8, addr)
     rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine(addr, addr, 4, 1, ctypes.cast(bad, ctypes.c_void_p),
-                                                              addr, 0, 2, addr, 0, None))
+                                                              nb, addr, 0, 2, addr, 0, 0, None))
     assert rc == _lib.QWZ_EINVAL and "16-byte aligned" in msg
+    rc, msg = _rc_and_msg(lib, lib.qwz_shard_exchange_combine_emulated(
+        addr, addr, 4, 4, 1, pv, nb + 1, addr, addr, 2, 0, 0, None))
+    assert rc == _lib.QWZ_EINVAL and "buffer_bytes" in msg
     rc, msg = _rc_and_msg(lib, lib.qwz_attn_shard_split(*([addr] * 11), 4, 1, 100, 256, 1, 4, 0.0625, 0, None))
     assert rc == _lib.QWZ_EINVAL and "tok_begin" in msg
 
@@ -169,3 +177,25 @@ def test_draft_prefill_ops_refuse_cpu_and_non_fp16():
     kv = torch.zeros(1, 16, 4, 256, dtype=torch.float16)
     with pytest.raises(ValueError, match="CUDA"):
         ops.draft_prefill(q, kv, kv, torch.empty_like(q))
+
+
+def test_graph_patch_argument_checks(lib):
+    count = ctypes.c_int32(-1)
+    rc, msg = _rc_and_msg(lib, lib.qwz_graph_kernel_nodes(None, 0, None, 0, ctypes.byref(count)))
+    assert rc == _lib.QWZ_EINVAL and "graph" in msg
+    buf = ctypes.create_string_buffer(64)
+    rc, msg = _rc_and_msg(lib, lib.qwz_graph_kernel_nodes(ctypes.addressof(buf), 7, None, 0, ctypes.byref(count)))
+    assert rc == _lib.QWZ_EINVAL and "kind" in msg
+    rc, msg = _rc_and_msg(lib, lib.qwz_graph_kernel_nodes(ctypes.addressof(buf), 0, None, 4, ctypes.byref(count)))
+    assert rc == _lib.QWZ_EINVAL and "nodes" in msg
+    p = ctypes.addressof(buf)
+    for args, needle in (((None, None, None, p, p, 0, 4, 8), "node"),
+                         ((None, None, p, None, p, 0, 4, 8), "block_table"),
+                         ((None, None, p, p, p, 0, 0, 8), "num_pages_per_seq"),
+                         ((None, None, p, p, p, 0, 4, 0), "num_splits"),
+                         ((None, None, p, p, p, 100, 4, 8), "split_len")):
+        rc, msg = _rc_and_msg(lib, lib.qwz_graph_patch_split(*args))
+        assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)
+    for args, needle in (((None, None, None, 4), "node"), ((None, None, p, 0), "num_splits")):
+        rc, msg = _rc_and_msg(lib, lib.qwz_graph_patch_combine(*args))
+        assert rc == _lib.QWZ_EINVAL and needle in msg, (needle, msg)

@@ -228,7 +228,7 @@ def test_c4_decode_262144_one_gpu_and_emulated_shards(cuda):
             lp = local[s.rank]
             ops.shard_split(q, kn, vn, lp[0], lp[1], lp[2], lp[3], ltab[:s.num_pages], lens,
                             po[s.rank], pml[s.rank], s.tok_begin, s.tok_span, splits)
-        ops.shard_exchange_combine_emulated(po, pml, splits, peers, epochs, res)
+        ops.shard_exchange_combine_emulated(po, pml, splits, peers, bufs[0].numel(), epochs, res)
         torch.cuda.synchronize()
         assert _lib.device_error(clear=True) == 0
         for g in range(world):

@@ -121,7 +121,7 @@ def test_peer_exchange_emulated_ranks_match_full_attention(cuda, world, total, d
             dc = local[s.rank]
             ops.shard_split(qd, kd, vd, dc["k_cache"], dc["v_cache"], dc["k_scales"], dc["v_scales"],
                             dc["table"], lens, po[s.rank], pml[s.rank], s.tok_begin, s.tok_span, splits)
-        ops.shard_exchange_combine_emulated(po, pml, splits, peers, epochs, out)
+        ops.shard_exchange_combine_emulated(po, pml, splits, peers, bufs[0].numel(), epochs, out)
         torch.cuda.synchronize()
         expect = oatt.nvfp4_attention(q.float(), **{k: v for k, v in to_cpu_torch(ref).items() if k != "table"},
                                       block_table=torch.from_numpy(table), pre_len=pre)
