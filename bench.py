@@ -360,6 +360,71 @@ def c5_record(device, stream, args, pk, splits_list=(16, 37)):
     return res
 
 
+K8V4_TOKEN_BYTES = 1664  # K 1,024 + V 512 + 2 x 64 B of FP16 scales per token (4 KV heads)
+
+
+def k8v4_layer(device, pages: int, tokens: int, seed: int):
+    """One K8/V4 layer of `tokens` seeded BF16 rows (4 outlier channels x8),
+    quantised by the library's writer into `pages` pages in a seed-permuted
+    order.  Returns (cache 4-tuple, block table)."""
+    from qwarz_b200 import k8v4
+
+    cache = k8v4.empty_cache(pages, device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    perm = torch.randperm(pages, generator=g, device=device).to(torch.int32)
+    outl = torch.randperm(DIM, generator=g, device=device)[:4]
+    for t0 in range(0, tokens, 16384):
+        n = min(16384, tokens - t0)
+        k = torch.randn(n, KV_HEADS, DIM, generator=g, device=device)
+        v = torch.randn(n, KV_HEADS, DIM, generator=g, device=device)
+        k[..., outl] *= 8.0
+        v[..., outl] *= 8.0
+        start = torch.tensor([t0], dtype=torch.int32, device=device)
+        k8v4.append(k.bfloat16(), v.bfloat16(), cache, perm, start)
+    return cache, perm
+
+
+def k8v4_record(device, stream, args, pk):
+    """The K8/V4 cache path (the reference's Attention64 split/combine slot):
+    decode at 65,536 tokens and MTP7 verify at 32,768 / 131,072, split alone
+    and split + rotating combine per layer, rotating over layers so the
+    pages exceed L2.  Algorithmic bytes: 1,664 B per token plus the table."""
+    from qwarz_b200 import k8v4, ops
+
+    res = {"token_bytes": K8V4_TOKEN_BYTES}
+    h32 = k8v4.hadamard32(device)
+    for tokens, layers, q_len in ((65536, 4, 1), (32768, 8, 7), (131072, 2, 7)):
+        pages = tokens // PAGE
+        lay = [k8v4_layer(device, pages, tokens, 9000 + l) for l in range(layers)]
+        g = torch.Generator(device=device).manual_seed(77)
+        q = [torch.randn(q_len, HEADS, DIM, generator=g, device=device).bfloat16() for _ in range(layers)]
+        out = [torch.empty_like(t) for t in q]
+        pre = torch.tensor([tokens - q_len], dtype=torch.int32, device=device)
+        splits = ops.default_splits(device, tokens, q_len)
+        po, pml = ops.split_workspace(device, q_len, splits)
+
+        def split_only():
+            for l in range(layers):
+                k8v4.split(q[l], lay[l][0], lay[l][1], pre, po, pml, h32, splits)
+
+        def call():
+            for l in range(layers):
+                k8v4.split(q[l], lay[l][0], lay[l][1], pre, po, pml, h32, splits)
+                k8v4.combine(po, pml, out[l], h32, splits)
+
+        ms_split = graph_ms(split_only, args.warmup, args.steps, stream) / layers
+        ms_call = graph_ms(call, args.warmup, args.steps, stream) / layers
+        byt = tokens * K8V4_TOKEN_BYTES + 4 * pages
+        res[f"{tokens}_q{q_len}"] = {
+            "tokens": tokens, "q_len": q_len, "layers_rotated": layers, "splits": splits,
+            "algorithmic_bytes_per_launch": byt, "split_us_per_launch": ms_split * 1e3,
+            "split_GBps": byt / (ms_split * 1e-3) / 1e9, "split_frac": byt / (ms_split * 1e-3) / 1e9 / pk["hbm_gbs"],
+            "call_us_per_layer": ms_call * 1e3}
+        del lay
+        torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------- N = 1: config 2
 def run_single(args, device) -> dict:
     from qwarz_b200 import attention as att
@@ -520,6 +585,7 @@ def run_single(args, device) -> dict:
         extras["c3_verify"] = c3_record(ops, device, stream, args, pk)
         extras["c4_262144_one_gpu"] = nvfp4_config(ops, device, stream, args, pk, C4_TOKENS, 4)["q1"]
         extras["c5_draft_fp8"] = c5_record(device, stream, args, pk)
+        extras["k8v4"] = k8v4_record(device, stream, args, pk)
         result["configs"] = extras
     return result
 
@@ -828,6 +894,8 @@ def run_extra(args, device) -> dict:
         res["configs"]["c4_262144_one_gpu"] = nvfp4_config(ops, device, stream, args, pk, C4_TOKENS, 4)["q1"]
     if args.workload in ("c5", "all"):
         res["configs"]["c5_draft_fp8"] = c5_record(device, stream, args, pk)
+    if args.workload in ("k8v4", "all"):
+        res["configs"]["k8v4"] = k8v4_record(device, stream, args, pk)
     return res
 
 
@@ -857,6 +925,21 @@ def run_profile_case(args, device) -> dict:
         ops.draft_prefill(qd, kd, vd, torch.empty_like(qd))
         torch.cuda.synchronize()
         return {"workload": args.workload, "tokens": S, "ok": True}
+    if args.workload == "profile_k8v4":
+        from qwarz_b200 import k8v4
+
+        cache, perm = k8v4_layer(device, pages, tokens, 9000)
+        q = torch.randn(1, HEADS, DIM, generator=g, device=device).bfloat16()
+        pre = torch.tensor([tokens - 1], dtype=torch.int32, device=device)
+        splits = ops.default_splits(device, tokens, 1)
+        po, pml = ops.split_workspace(device, 1, splits)
+        out = torch.empty_like(q)
+        h32 = k8v4.hadamard32(device)
+        for _ in range(3):
+            k8v4.split(q, cache, perm, pre, po, pml, h32, splits)
+            k8v4.combine(po, pml, out, h32, splits)
+        torch.cuda.synchronize()
+        return {"workload": args.workload, "tokens": tokens, "ok": True}
     if args.workload == "profile_draft":
         T = tokens + 6
         k8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
@@ -971,10 +1054,10 @@ def main():
                          "rank can reach every GPU, else NCCL)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c3", "c4", "c5", "prefill", "all", "profile_prefill", "profile_decode",
-                             "profile_verify", "profile_draft"],
+                    choices=["auto", "c3", "c4", "c5", "k8v4", "prefill", "all", "profile_prefill",
+                             "profile_decode", "profile_verify", "profile_draft", "profile_k8v4"],
                     help="auto: the driver's headline (config 2 at N=1 with sub-records, config 4 "
-                         "split over the N GPUs at N>1); c3/c4/c5/prefill/all: single-GPU configs "
+                         "split over the N GPUs at N>1); c3/c4/c5/k8v4/prefill/all: single-GPU configs "
                          "(separate JSON); profile_*: three eager launches of one kernel on one "
                          "65,536-token layer, the small case for ncu --set full")
     args = ap.parse_args()

@@ -348,6 +348,52 @@ int qwz_nvfp4_gather(const void* packed, const void* scales, const int32_t* bloc
                      int32_t table_width, int32_t n_heads, int32_t head_dim, int32_t page_size,
                      void* stream);
 
+/*
+ * K8/V4 cache path: the cache of the reference's Attention64 split/combine
+ * slot and of its MTP draft (ExLlamaV3 CacheLayer_quant, k_bits 8, v_bits 4;
+ * src/qwasar_runtime/xqa.py:926-961).  Geometry as
+ * src/qwasar_bench/prefill_flash.py:32-44 checks it:
+ *   k_cache int32 [P, 256, 256], v_cache int32 [P, 256, 128],
+ *   k_scales / v_scales FP16 [P, 256, 32].
+ * A (token, KV head h, 32-dim block j) holds 32 codes of b bits (8 for K, 4
+ * for V) as b bit-plane words (word i = bit i of the codes, bit t = element
+ * t) at (h * 8 + j) * b of the token's row, and one FP16 scale at h * 8 + j,
+ * in the rotated domain R = H32 / sqrt(32).  The reader is
+ *   x_rot = FP16((FP32(c) - (2^(b-1) - 0.5)) * (FP32(s) / 2^(b-1)))
+ * (docs/superpowers/specs/2026-09-08-direct-k8v4-attention-design.md:55-61).
+ *
+ * qwz_k8v4_append  quantises rows k, v [append_len, 4, 256] (FP16/BF16) at
+ *                  logical positions cache_seqlens[0] + s: each 32-dim block
+ *                  is rotated by the natural-order Hadamard butterfly (FP32),
+ *                  s = FP16(max |x_rot|), c = clamp(floor(x_rot / s *
+ *                  2^(b-1) + 2^(b-1)), 0, 2^b - 1).
+ * qwz_k8v4_split   the split kernel with the reference's 15 + 2 argument
+ *                  order (docs/superpowers/specs/2026-09-11-qwasar-attention-
+ *                  kernel.md:62-74; same tail as qwz_attn_split): h32 is the
+ *                  rotation R, FP32 [32, 32] row-major (required); sinks must
+ *                  be NULL.  The partials are in the rotated domain, in the
+ *                  layout of qwz_attn_split.  num_pages bounds the pool.
+ * qwz_k8v4_combine the combine with the reference combine order: merges the
+ *                  partials and writes out = R^T O per 32-dim block.
+ * qwz_k8v4_gather  the reader alone: logical tokens [0, length) of one cache
+ *                  (bits 8 for K, 4 for V) into FP16 [length, 4, 256],
+ *                  rotated domain.
+ */
+int qwz_k8v4_append(const void* k, const void* v, void* k_cache, void* v_cache, void* k_scales,
+                    void* v_scales, const int32_t* block_table, const int32_t* cache_seqlens,
+                    int32_t table_width, int32_t num_pages, int32_t append_len, int32_t dtype,
+                    void* stream);
+int qwz_k8v4_split(const void* q, const void* k_cache, const void* v_cache, const int32_t* block_table,
+                   const int32_t* cache_seqlens, void* out, float* partial_o, float* partial_ml,
+                   const void* k_scales, const void* v_scales, const void* h32, int32_t split_len,
+                   int32_t num_pages_per_seq, int32_t num_splits, const void* sinks, void* global_scratch,
+                   void* profile_scratch, int32_t q_len, int32_t num_pages, float sm_scale, int32_t dtype,
+                   void* stream);
+int qwz_k8v4_combine(const float* partial_o, const float* partial_ml, void* out, const void* h32,
+                     int32_t num_splits, const void* sinks, int32_t q_len, int32_t dtype, void* stream);
+int qwz_k8v4_gather(const void* words, const void* scales, const int32_t* block_table, int32_t table_width,
+                    int32_t num_pages, int32_t length, int32_t bits, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,9 @@ Modules
   attention  FP32 softmax attention with the reference's lower-right causal
              mask and GQA (restates xqa.py:612-673), the draft split-K and
              its LSE merge (engine/forward/draft_attention.py:23-79)
+  k8v4       the K8/V4 quantised cache (bit planes, Hadamard-rotated
+             blocks, the reader formula of the reference's K8/V4 design) and
+             FP32 attention over it
   rng        a version-independent seeded byte/float stream for fixtures
 
 Pinning.  The dequant and the attention are pinned by golden vectors that

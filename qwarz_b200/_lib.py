@@ -53,6 +53,10 @@ SIGNATURES = {
     "qwz_graph_kernel_nodes": [c_void_p, c_int32, c_void_p, c_int32, _i32p],
     "qwz_graph_patch_split": [c_void_p] * 5 + [c_int32] * 3,
     "qwz_graph_patch_combine": [c_void_p] * 3 + [c_int32],
+    "qwz_k8v4_append": [c_void_p] * 8 + [c_int32] * 4 + [c_void_p],
+    "qwz_k8v4_split": [c_void_p] * 11 + [c_int32] * 3 + [c_void_p] * 3 + [c_int32, c_int32, c_float, c_int32, c_void_p],
+    "qwz_k8v4_combine": [c_void_p] * 4 + [c_int32, c_void_p, c_int32, c_int32, c_void_p],
+    "qwz_k8v4_gather": [c_void_p] * 3 + [c_int32] * 4 + [c_void_p, c_void_p],
     "qwz_shard_exchange_combine_emulated": [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p,
                                             c_int64, c_void_p, c_void_p, c_int32, c_int64, c_int32,
                                             c_void_p],

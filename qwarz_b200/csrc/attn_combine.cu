@@ -12,7 +12,10 @@
 // split), and the next kernel in the stream may begin its launch as soon as
 // the combine starts (programmatic dependent launch).  The same kernel
 // reduces a shard's local splits to one (m, l, O) record (partial mode) and
-// combines the all-gathered records of the sequence-sharded decode.
+// combines the all-gathered records of the sequence-sharded decode.  In
+// rotate mode (the K8/V4 cache, whose partials are in the rotated domain
+// R = H32 / sqrt(32)) the merged row is restored as out = R^T O per 32-dim
+// block, R being the caller's h32 matrix.
 
 #include "qwz_common.cuh"
 #include "qwz_kernels.h"
@@ -32,6 +35,12 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const CombineParams p)
   const int tid = threadIdx.x, grp = tid >> 5, lane = tid & 31;
   griddep_wait();               // the partials come from the previous kernel
   griddep_launch_dependents();  // the next kernel may begin its launch
+  constexpr int kRotPitch = 33;
+  __shared__ float rot_h[MODE == kCombineRotate ? 32 * kRotPitch : 1];
+  __shared__ float rot_v[MODE == kCombineRotate ? kHeadDim : 1];
+  if constexpr (MODE == kCombineRotate) {
+    for (int k = tid; k < 1024; k += 256) rot_h[(k >> 5) * kRotPitch + (k & 31)] = __ldg(p.h32 + k);
+  }
   const float* ml = p.pml + (long long)row * p.ml_row;
   const float* po = p.po + (long long)row * p.o_row + lane * 8;
   const int S = p.num_splits;
@@ -118,6 +127,16 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const CombineParams p)
   if constexpr (MODE == kCombineFinal) {
     TOut* out = reinterpret_cast<TOut*>(p.out) + (long long)row * kHeadDim;
     out[d] = InTraits<TOut>::from_float(L > 0.f ? o / L : 0.f);
+  } else if constexpr (MODE == kCombineRotate) {
+    rot_v[d] = L > 0.f ? o / L : 0.f;
+    __syncthreads();
+    // out_i = sum_j R[j][i] O_j within the block (a warp is one block)
+    const int b = d >> 5, i = d & 31;
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc = fmaf(rot_h[j * kRotPitch + i], rot_v[b * 32 + j], acc);
+    TOut* out = reinterpret_cast<TOut*>(p.out) + (long long)row * kHeadDim;
+    out[d] = InTraits<TOut>::from_float(acc);
   } else {
     float* out = reinterpret_cast<float*>(p.out) + (long long)row * (kHeadDim + 2);
     out[2 + d] = o;
@@ -134,6 +153,10 @@ cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStre
   // partials only after griddep_wait()
   const dim3 grid(p.rows), block(256);
   if (mode == kCombinePartial) return launch_pdl(lse_combine_kernel<float, kCombinePartial>, grid, block, 0, stream, p);
+  if (mode == kCombineRotate) {
+    if (dtype == kDtypeBF16) return launch_pdl(lse_combine_kernel<__nv_bfloat16, kCombineRotate>, grid, block, 0, stream, p);
+    return launch_pdl(lse_combine_kernel<__half, kCombineRotate>, grid, block, 0, stream, p);
+  }
   if (dtype == kDtypeBF16) return launch_pdl(lse_combine_kernel<__nv_bfloat16, kCombineFinal>, grid, block, 0, stream, p);
   return launch_pdl(lse_combine_kernel<__half, kCombineFinal>, grid, block, 0, stream, p);
 }

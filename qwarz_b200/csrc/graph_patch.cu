@@ -31,6 +31,18 @@ bool is_split_kernel(const void* f) {
       reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 16>),
       reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 32>),
       reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 48>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 1>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 2>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 3>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 4>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 5>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 6>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 1>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 2>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 3>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 4>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 5>),
+      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 6>),
   };
   for (const void* k : known)
     if (k == f) return true;
@@ -43,6 +55,8 @@ bool is_combine_kernel(const void* f) {
       reinterpret_cast<const void*>(lse_combine_kernel<__half, kCombineFinal>),
       reinterpret_cast<const void*>(lse_combine_kernel<__nv_bfloat16, kCombineFinal>),
       reinterpret_cast<const void*>(lse_combine_kernel<float, kCombinePartial>),
+      reinterpret_cast<const void*>(lse_combine_kernel<__half, kCombineRotate>),
+      reinterpret_cast<const void*>(lse_combine_kernel<__nv_bfloat16, kCombineRotate>),
   };
   for (const void* k : known)
     if (k == f) return true;

@@ -49,6 +49,9 @@ struct alignas(64) SplitParams {
   // are FP16 [4, 256] rows for store slot app_slot[0]; the CTA whose stage
   // holds that slot writes it to the store and into its shared-memory copy.
   const int32_t* app_slot;
+  // K8/V4 split (k8v4.cu): the rotation R, FP32 [32, 32] row-major; the
+  // codes are int32 bit-plane words and the scales FP16.
+  const float* h32;
 };
 
 // NVFP4 paged prefill attention (attn_prefill.cu): q [q_len, 24, 256] over
@@ -78,9 +81,25 @@ struct CombineParams {
   int rows;
   int num_splits;
   void* out;          // final: [rows, 256] FP16/BF16 ; partial: [rows, 258] FP32 (m, l, O)
+  const float* h32;   // rotate mode: R, FP32 [32, 32]; out = R^T O per 32-dim block
 };
 
-enum : int { kCombineFinal = 0, kCombinePartial = 1 };
+enum : int { kCombineFinal = 0, kCombinePartial = 1, kCombineRotate = 2 };
+
+// K8/V4 writer (k8v4.cu): new rows at logical positions seqlens[0] + s.
+struct K8v4AppendParams {
+  const void* k;                 // [S, 4, 256] FP16/BF16
+  const void* v;
+  uint32_t* k_cache;             // [P, 256, 256] bit-plane words
+  uint32_t* v_cache;             // [P, 256, 128]
+  __half* k_scales;              // [P, 256, 32]
+  __half* v_scales;
+  const int32_t* block_table;
+  const int32_t* seqlens;        // pre-append length [1]
+  int table_width;
+  int num_pages;
+  int append_len;
+};
 
 struct AppendParams {
   const void* k;                 // [S, kv_heads, 256] new rows
@@ -146,5 +165,9 @@ cudaError_t launch_combine(const CombineParams& p, int mode, int dtype, cudaStre
 cudaError_t launch_nvfp4_append(const AppendParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_fp8_write(const Fp8WriteParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_nvfp4_gather(const GatherParams& p, cudaStream_t stream);
+cudaError_t launch_k8v4_split(const SplitParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_k8v4_append(const K8v4AppendParams& p, int dtype, cudaStream_t stream);
+cudaError_t launch_k8v4_gather(const uint32_t* words, const __half* scales, const int32_t* table, int width,
+                               int num_pages, int length, int bits, __half* out, cudaStream_t stream);
 
 }  // namespace qwz

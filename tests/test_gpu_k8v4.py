@@ -1,0 +1,234 @@
+"""K8/V4 cache path on the GPU (csrc/k8v4.cu) against the restatement in
+oracle/k8v4.py.
+
+* writer: the bit-plane words and FP16 scales of appended rows equal the
+  oracle writer's bit for bit (FP16 and BF16 rows, a page crossing, a zero
+  block, values beyond the FP16 range), and nothing else is touched;
+* reader: the device gather equals the reference's reader formula bit for
+  bit over random words and edge scales (0, subnormal, 65504);
+* attention: append + split + combine against the FP32 oracle over the same
+  cache, for the reference's length matrix 7 / 31 / 32 / 255 / 256 / 257 /
+  4093 (docs/superpowers/plans/2026-09-08-direct-k8v4-attention.md:91) and
+  q_len 1..8, with permuted tables, empty splits and both rotation paths
+  (the Hadamard butterfly and the general h32 matrix);
+* graph replay with a mutated device length and a swapped table, against
+  eager calls (the reference's gate, same plan :93);
+* the ABI's refusals (h32 NULL, sinks non-NULL).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import k8v4 as ok8, rng
+from tests.conftest import err_stats
+from tests.golden import cases
+
+pytestmark = pytest.mark.gpu
+
+DT = {"float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+def _dev_cache(c: dict, device):
+    return (torch.from_numpy(c["k_cache"].copy()).to(device), torch.from_numpy(c["v_cache"].copy()).to(device),
+            torch.from_numpy(c["k_scales"].copy()).to(device), torch.from_numpy(c["v_scales"].copy()).to(device))
+
+
+def _same_cache(dev, c: dict):
+    names = ("k_cache", "v_cache", "k_scales", "v_scales")
+    for t, name in zip(dev, names):
+        a = t.cpu().numpy()
+        b = c[name]
+        if a.dtype == np.float16:
+            a, b = a.view(np.uint16), b.view(np.uint16)
+        assert np.array_equal(a, b), name
+
+
+def _rows(seed, n, dtype):
+    """Rows as the device will see them (rounded to dtype) and their float32 values."""
+    x = torch.from_numpy(cases.kv_rows(seed, n, 4)).to(DT[dtype])
+    return x, x.float().numpy()
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_writer_bit_exact(cuda, dtype):
+    from qwarz_b200 import k8v4
+
+    P, pre, S = 3, 237, 300  # the rows cross from the first page into the second
+    table = rng.permutation(31, P)
+    kt, kf = _rows(40, S, dtype)
+    vt, vf = _rows(41, S, dtype)
+    kt[0, 1, :32] = 0  # a zero block: scale 0, every code 2^(b-1)
+    kt[1, 2, 5] = 3.0e4 if dtype == "float16" else 1.0e6  # beyond FP16 in BF16: the scale clamps to 65504
+    kf = kt.float().numpy()
+    ref = ok8.empty_cache(P)
+    ok8.write_rows(ref, kf, vf, table, pre)
+    dev = k8v4.empty_cache(P, cuda)
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    k8v4.append(kt.to(cuda), vt.to(cuda), dev, torch.from_numpy(table).to(cuda), lens)
+    torch.cuda.synchronize()
+    _same_cache(dev, ref)
+    from qwarz_b200 import _lib
+
+    assert _lib.device_error(clear=True) == 0
+
+
+def test_reader_equals_the_formula(cuda):
+    from qwarz_b200 import k8v4
+
+    P, L = 2, 400
+    table = np.array([1, 0], np.int32)
+    c = ok8.empty_cache(P)
+    c["k_cache"][:] = rng.bytes_(50, c["k_cache"].nbytes).view(np.int32).reshape(c["k_cache"].shape)
+    c["v_cache"][:] = rng.bytes_(51, c["v_cache"].nbytes).view(np.int32).reshape(c["v_cache"].shape)
+    edge = np.array([0.0, 2.0 ** -24, 6.1e-5, 0.0078125, 0.37, 1.0, 3.5, 1000.0, 65504.0], np.float16)
+    c["k_scales"][:] = edge[rng.bytes_(52, c["k_scales"].size) % edge.size].reshape(c["k_scales"].shape)
+    c["v_scales"][:] = edge[rng.bytes_(53, c["v_scales"].size) % edge.size].reshape(c["v_scales"].shape)
+    kc, vc, ks, vs = _dev_cache(c, cuda)
+    t = torch.from_numpy(table).to(cuda)
+    for words, scales, name, bits in ((kc, ks, "k", 8), (vc, vs, "v", 4)):
+        got = k8v4.gather(words, scales, t, L, bits).cpu().numpy()
+        ref = ok8.gather_rotated(c[f"{name}_cache"], c[f"{name}_scales"], table, L, bits)
+        assert np.array_equal(got.view(np.uint16), ref.view(np.uint16)), name
+
+
+# Tolerance.  The K8/V4 path is held to the reference's own gate for it:
+# relative L2 <= 3e-3 against the FP32 oracle over the same dequantised cache
+# (docs/superpowers/plans/2026-09-08-direct-k8v4-attention.md:92), and, so that
+# no row hides behind the aggregate, every (query row, head) vector within
+# max|err| <= 1e-2 * max|ref| of that vector.  The element-wise 2e-3 bound of
+# the NVFP4 tests does not apply: the output is restored from the rotated
+# domain, so the FP16 rounding of a block's rotated values is spread over all
+# 32 of its dims, small ones included.
+REL_L2 = 3e-3
+VEC_REL = 1e-2
+
+
+def assert_close_rotated(out, ref, what=""):
+    out = np.asarray(out, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    assert np.isfinite(out).all(), f"{what}: non-finite output"
+    max_abs, _, rel_l2 = err_stats(out, ref)
+    d = np.abs(out - ref).reshape(-1, 256).max(1)
+    vec = float((d / np.maximum(np.abs(ref).reshape(-1, 256).max(1), 1e-30)).max())
+    assert rel_l2 <= REL_L2 and vec <= VEC_REL, f"{what}: rel_l2={rel_l2:.3e} vec_rel={vec:.3e} max_abs={max_abs:.3e}"
+
+
+def _attend_case(cuda, q_len, total, dtype, splits=None, general=False, seed=0):
+    from qwarz_b200 import k8v4, ops
+
+    pre = total - q_len
+    P = (total + 255) // 256 + 1
+    table = rng.permutation(60 + seed, P)
+    kt = torch.from_numpy(cases.kv_rows(61 + seed, total, 4)).to(DT[dtype])
+    vt = torch.from_numpy(cases.kv_rows(62 + seed, total, 4)).to(DT[dtype])
+    kf, vf = kt.float().numpy(), vt.float().numpy()
+    ref = ok8.empty_cache(P)
+    ok8.write_rows(ref, kf[:pre], vf[:pre], table, 0)
+    dev = _dev_cache(ref, cuda)
+    ok8.write_rows(ref, kf[pre:], vf[pre:], table, pre)  # what the device append must produce
+    q = torch.from_numpy(rng.normal(63 + seed, q_len * 24 * 256).astype(np.float32).reshape(q_len, 24, 256)).to(DT[dtype])
+    h32 = k8v4.hadamard32(cuda)
+    if general:  # off by one ulp: not the exact Hadamard, so the kernel takes the matrix path
+        h32 = torch.nextafter(h32, torch.zeros_like(h32))
+    splits = splits or ops.default_splits(cuda, total, q_len)
+    po, pml = ops.split_workspace(cuda, q_len, splits)
+    out = torch.empty(q_len, 24, 256, dtype=DT[dtype], device=cuda)
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    k8v4.attend(q.to(cuda), kt[pre:].to(cuda), vt[pre:].to(cuda), dev, torch.from_numpy(table).to(cuda), lens, out,
+                po, pml, h32, splits)
+    torch.cuda.synchronize()
+    _same_cache(dev, ref)
+    oref = ok8.attention(q, ref, table, pre)
+    return out.float().cpu().numpy(), oref.numpy()
+
+
+@pytest.mark.parametrize("total", [7, 31, 32, 255, 256, 257, 4093])
+@pytest.mark.parametrize("q_len", [1, 2, 7, 8])
+def test_attention_length_matrix(cuda, q_len, total):
+    if q_len > total:
+        pytest.skip("q_len beyond the length")
+    out, ref = _attend_case(cuda, q_len, total, "float16", seed=total % 17 + q_len)
+    assert_close_rotated(out, ref, f"k8v4 q_len={q_len} total={total}")
+    from qwarz_b200 import _lib
+
+    assert _lib.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("q_len", [3, 4, 5, 6])
+def test_attention_every_row_tile(cuda, q_len):
+    out, ref = _attend_case(cuda, q_len, 3000, "bfloat16", seed=q_len)
+    assert_close_rotated(out, ref, f"k8v4 q_len={q_len}")
+
+
+def test_attention_empty_splits_and_general_rotation(cuda):
+    # 70 splits over 5 stages of 128 tokens: most splits own nothing
+    out, ref = _attend_case(cuda, 7, 600, "float16", splits=70, seed=3)
+    assert_close_rotated(out, ref, "k8v4 empty splits")
+    out, ref = _attend_case(cuda, 7, 2000, "float16", general=True, seed=4)
+    assert_close_rotated(out, ref, "k8v4 general h32")
+
+
+def test_long_context(cuda):
+    out, ref = _attend_case(cuda, 7, 32768, "bfloat16", seed=5)
+    assert_close_rotated(out, ref, "k8v4 32K q_len 7")
+
+
+def test_graph_replay_with_mutated_length_and_table(cuda):
+    from qwarz_b200 import k8v4, ops
+
+    P, total, q_len = 20, 4093, 7
+    table = rng.permutation(70, P)
+    kt = torch.from_numpy(cases.kv_rows(71, P * 256, 4)).half()
+    vt = torch.from_numpy(cases.kv_rows(72, P * 256, 4)).half()
+    c = ok8.empty_cache(P)
+    ok8.write_rows(c, kt.float().numpy(), vt.float().numpy(), table, 0)  # every slot filled
+    dev = _dev_cache(c, cuda)
+    before = [t.clone() for t in dev]
+    q = torch.from_numpy(rng.normal(73, q_len * 24 * 256).astype(np.float32).reshape(q_len, 24, 256)).half().to(cuda)
+    h32 = k8v4.hadamard32(cuda)
+    splits = 37
+    po, pml = ops.split_workspace(cuda, q_len, splits)
+    lens = torch.tensor([1000], dtype=torch.int32, device=cuda)
+    t_dev = torch.from_numpy(table).to(cuda)
+    out = torch.empty(q_len, 24, 256, dtype=torch.half, device=cuda)
+
+    def step():
+        k8v4.split(q, dev, t_dev, lens, po, pml, h32, splits)
+        k8v4.combine(po, pml, out, h32, splits)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    other = rng.permutation(74, P)
+    for pre, tab in ((total - q_len, table), (511, table), (512, table), (2049, other), (1000, table)):
+        lens.fill_(pre)
+        t_dev.copy_(torch.from_numpy(tab))
+        g.replay()
+        torch.cuda.synchronize()
+        replay = out.clone()
+        step()
+        torch.cuda.synchronize()
+        assert torch.equal(replay, out), pre
+        ref = ok8.attention(q.cpu(), c, tab, pre)
+        assert_close_rotated(out.float().cpu().numpy(), ref.numpy(), f"graph pre={pre}")
+    for a, b in zip(dev, before):  # the reader writes nothing
+        assert torch.equal(a, b)
+
+
+def test_abi_refusals(cuda):
+    from qwarz_b200 import _lib
+
+    lib = _lib.load()
+    x = torch.zeros(1024, dtype=torch.float32, device=cuda)
+    p = x.data_ptr()
+    args = [p, p, p, p, p, None, p, p, p, p]
+    rc = lib.qwz_k8v4_split(*args, None, 0, 1, 1, None, None, None, 1, 1, 0.0625, 0, None)
+    assert rc == _lib.QWZ_EINVAL and b"h32" in lib.qwz_last_error()
+    rc = lib.qwz_k8v4_split(*args, p, 0, 1, 1, p, None, None, 1, 1, 0.0625, 0, None)
+    assert rc == _lib.QWZ_EINVAL and b"sinks" in lib.qwz_last_error()
+    rc = lib.qwz_k8v4_combine(p, p, p, None, 1, None, 1, 0, None)
+    assert rc == _lib.QWZ_EINVAL and b"h32" in lib.qwz_last_error()
