@@ -43,6 +43,8 @@ bool is_split_kernel(const void* f) {
       reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 4>),
       reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 5>),
       reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 6>),
+      reinterpret_cast<const void*>(k8v4_decode16_kernel<__half>),
+      reinterpret_cast<const void*>(k8v4_decode16_kernel<__nv_bfloat16>),
   };
   for (const void* k : known)
     if (k == f) return true;

@@ -17,11 +17,11 @@
 //      one (m, l, O) record;
 //   2. stores it, tagged with e = this row's call count, into every rank's
 //      buffer at [g][r] (stores into the peers' memory);
-//   3. reads the world records of row r from its own buffer, waiting per
-//      word until it carries epoch e (bounded by globaltimer, p.timeout_ns
-//      for the whole row: a timeout sets kErrTimeout and merges what is
-//      there), and merges them in rank order, so every rank writes the same
-//      output.
+//   3. reads the world records of row r from its own buffer, all ranks'
+//      words in one batch of loads per poll, until every word carries epoch
+//      e (bounded by globaltimer, p.timeout_ns for the whole row: a timeout
+//      sets kErrTimeout and merges the records that did arrive), and merges
+//      them in rank order, so every rank writes the same output.
 // Epochs count calls per row on every rank (a device word per row, advanced
 // by the kernel), so repeated launches and CUDA-graph replays need no reset.
 // With fewer GPUs than ranks the kernel runs all ranks in one cooperative
@@ -53,25 +53,6 @@ QWZ_DEVINL uint64_t ld_tagged(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
-// The value of a tagged word once it carries epoch e; false once
-// timeout_ns have passed since t0.
-QWZ_DEVINL bool wait_tagged(const uint64_t* p, uint32_t e, uint64_t t0, uint64_t timeout_ns, float& v) {
-  for (int i = 0;; ++i) {
-    const uint64_t w = ld_tagged(p);
-    if ((uint32_t)(w >> 32) == e) {
-      v = __uint_as_float((uint32_t)w);
-      return true;
-    }
-    if ((i & 63) == 63) {
-      if (global_ns() - t0 > timeout_ns) {
-        v = __uint_as_float((uint32_t)w);
-        return false;
-      }
-      __nanosleep(32);
-    }
-  }
-}
-
 }  // namespace
 
 template <typename TOut>
@@ -176,20 +157,52 @@ __global__ void __launch_bounds__(256) shard_exchange_kernel(const ExchangeParam
   }
 
   // --------------------------------------- 3. wait for all, merge, write
+  // Every rank's three words of this thread are loaded in one batch (the
+  // loads are independent, so they are in flight together: one round trip
+  // per poll, not one per rank); only the words whose epoch is still old
+  // are loaded again.
   const uint64_t* local = reinterpret_cast<const uint64_t*>(p.peers[rank]);
   const uint64_t t0 = global_ns();
   bool ok = true;
   float mg[kMaxWorld], lg[kMaxWorld], og[kMaxWorld];
+  uint64_t wm[kMaxWorld], wl[kMaxWorld], wo[kMaxWorld];
+  uint32_t pending = 0u;  // bit g: rank g's words are not all of epoch e yet
 #pragma unroll
   for (int g = 0; g < kMaxWorld; ++g) {
-    mg[g] = -CUDART_INF_F;
-    lg[g] = og[g] = 0.f;
-    if (g < p.world) {
-      const uint64_t* src = local + half + ((size_t)g * rows + r) * kRecWords;
-      ok &= wait_tagged(src, e, t0, p.timeout_ns, mg[g]);
-      ok &= wait_tagged(src + 1, e, t0, p.timeout_ns, lg[g]);
-      ok &= wait_tagged(src + 2 + tid, e, t0, p.timeout_ns, og[g]);
+    wm[g] = wl[g] = wo[g] = 0ull;
+    if (g < p.world) pending |= 1u << g;
+  }
+  for (int i = 0; pending; ++i) {
+#pragma unroll
+    for (int g = 0; g < kMaxWorld; ++g) {
+      if (pending & (1u << g)) {
+        const uint64_t* src = local + half + ((size_t)g * rows + r) * kRecWords;
+        wm[g] = ld_tagged(src);
+        wl[g] = ld_tagged(src + 1);
+        wo[g] = ld_tagged(src + 2 + tid);
+      }
     }
+#pragma unroll
+    for (int g = 0; g < kMaxWorld; ++g) {
+      if ((pending & (1u << g)) && (uint32_t)(wm[g] >> 32) == e && (uint32_t)(wl[g] >> 32) == e &&
+          (uint32_t)(wo[g] >> 32) == e)
+        pending &= ~(1u << g);
+    }
+    if (pending && (i & 63) == 63) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxWorld; ++g) {
+    // ranks whose record never arrived merge as empty (m = -inf)
+    const bool have = g < p.world && !(pending & (1u << g));
+    mg[g] = have ? __uint_as_float((uint32_t)wm[g]) : -CUDART_INF_F;
+    lg[g] = have ? __uint_as_float((uint32_t)wl[g]) : 0.f;
+    og[g] = have ? __uint_as_float((uint32_t)wo[g]) : 0.f;
   }
   if (!ok) flag_error(kErrTimeout);
   float Mg = -CUDART_INF_F;

@@ -232,3 +232,70 @@ def test_abi_refusals(cuda):
     assert rc == _lib.QWZ_EINVAL and b"sinks" in lib.qwz_last_error()
     rc = lib.qwz_k8v4_combine(p, p, p, None, 1, None, 1, 0, None)
     assert rc == _lib.QWZ_EINVAL and b"h32" in lib.qwz_last_error()
+
+
+def test_graph_patch_of_k8v4_split_and_combine_nodes(cuda):
+    """The reference's graph patches split arguments 3, 4, 11, 12, 13 and
+    combine argument 4 of this slot between replays
+    (docs/superpowers/specs/2026-09-11-qwasar-attention-kernel.md:66-74):
+    captured K8/V4 split and combine nodes take the same patches, and every
+    patched replay equals eager launches with the same arguments."""
+    from qwarz_b200 import _lib, k8v4, ops
+    from qwarz_b200.contract import backend
+
+    P, q_len = 16, 7
+    table_a = rng.permutation(90, P)
+    kt = torch.from_numpy(cases.kv_rows(91, P * 256, 4)).half()
+    vt = torch.from_numpy(cases.kv_rows(92, P * 256, 4)).half()
+    c = ok8.empty_cache(P)
+    ok8.write_rows(c, kt.float().numpy(), vt.float().numpy(), table_a, 0)
+    dev = _dev_cache(c, cuda)
+    q = torch.from_numpy(rng.normal(93, q_len * 24 * 256).astype(np.float32).reshape(q_len, 24, 256)).half().to(cuda)
+    h32 = k8v4.hadamard32(cuda)
+    t_a = torch.from_numpy(table_a).to(cuda)
+    t_b = torch.from_numpy(rng.permutation(94, P)).to(cuda)
+    lens_a = torch.tensor([3500], dtype=torch.int32, device=cuda)
+    lens_b = torch.tensor([3700 - q_len], dtype=torch.int32, device=cuda)
+    po, pml = ops.split_workspace(cuda, q_len, 37)
+    out = torch.empty_like(q)
+
+    def launch(table, lens, splits, split_len, o, p_o, p_ml):
+        k8v4.split(q, dev, table, lens, p_o, p_ml, h32, splits, split_len)
+        k8v4.combine(p_o, p_ml, o, h32, splits)
+
+    def eager(table, lens, splits, split_len):
+        o = torch.empty_like(q)
+        p_o, p_ml = ops.split_workspace(cuda, q_len, splits)
+        launch(table, lens, splits, split_len, o, p_o, p_ml)
+        torch.cuda.synchronize()
+        return o
+
+    launch(t_a, lens_a, 37, 0, out, po, pml)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph(keep_graph=True)
+    with torch.cuda.graph(g):
+        launch(t_a, lens_a, 37, 0, out, po, pml)
+    g.instantiate()
+    graph = g.raw_cuda_graph()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager(t_a, lens_a, 37, 0))
+    s_nodes = backend.graph_nodes(graph, _lib.NODE_SPLIT)
+    c_nodes = backend.graph_nodes(graph, _lib.NODE_COMBINE)
+    assert len(s_nodes) == 1 and len(c_nodes) == 1
+    for table, lens, splits, split_len, width, exec_too in (
+            (t_b, lens_b, 20, 0, 15, True),
+            (t_b, lens_b, 8, 512, 15, True),
+            (t_a, lens_a, 37, 0, P, False)):
+        packed = backend.pack_split_args({"block_table": table.data_ptr(), "cache_seqlens": lens.data_ptr()},
+                                         {"split_len": split_len, "num_pages_per_seq": width, "num_splits": splits})
+        exe = g.raw_cuda_graph_exec() if exec_too else None
+        backend.patch_split(graph, exe, s_nodes[0], packed)
+        backend.patch_combine(graph, exe, c_nodes[0], splits)
+        if not exec_too:
+            g.instantiate()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager(table[:width], lens, splits, split_len)), (splits, split_len, exec_too)
+    assert _lib.device_error(clear=True) == 0
+    del g

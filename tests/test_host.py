@@ -213,3 +213,15 @@ def test_bench_algorithmic_bytes_per_layer_call():
         got = bench.layer_bytes(L, q_len)
         assert got == expect(L, q_len)
         assert abs(got / 1e6 - mb) < 0.01, (L, q_len, got)
+
+
+def test_bench_k8v4_token_bytes_follow_the_cache_geometry():
+    """The K8/V4 record's algorithmic bytes per token: the bit-plane words of
+    K (4 heads x 8 blocks x 8 planes x 4 B) and V (x 4 planes) and the two
+    FP16 scale rows (4 x 8 each), as the cache tensors hold them."""
+    import bench
+    from qwarz_b200 import k8v4
+
+    kc, vc, ks, vs = k8v4.empty_cache(1, "cpu")
+    per_token = sum(t[0, 0].numel() * t.element_size() for t in (kc, vc, ks, vs))
+    assert per_token == bench.K8V4_TOKEN_BYTES == 1664
