@@ -31,8 +31,7 @@ value  = whole-job algorithmic HBM bytes per step / device step time (GB/s);
          per layer call 1152*L + 2*(24*256*2) + 4*P + 1152 + 2*4*256*2 bytes.
 e2e    = the same bytes through the public API a caller uses, with every
          step's Q/K/V copied in from pinned host memory and the outputs copied
-         back inside the timed region (one H2D per step, one D2H per layer on
-         a copy stream that overlaps the later layers): qwarz_b200.attention.attend per layer
+         back inside the timed region: qwarz_b200.attention.attend per layer
          (N = 1), captured in the caller's CUDA graph as the engine does;
          ShardedDecode.step per layer (N > 1).
 roofline: the split kernel alone (a graph of its 16 launches), CUDA events.
@@ -467,7 +466,7 @@ def run_single(args, device) -> dict:
     # ----- end to end through the drop-in: qwarz_b200.attention.attend per
     # layer (validation, the adapter's persistent output buffer, one append +
     # split + combine), inside the caller's CUDA graph as the engine captures
-    # its forward; one pinned H2D of the step's q/k/v, one D2H per layer output.
+    # its forward; one pinned H2D of the step's q/k/v, one D2H of the outputs.
     per_in = HEADS * DIM + 2 * KV_HEADS * DIM
     host_in = torch.empty(LAYERS, per_in, dtype=torch.bfloat16).pin_memory()
     for l in range(LAYERS):
@@ -480,25 +479,16 @@ def run_single(args, device) -> dict:
     tables = [perm.view(1, -1) for _, perm in layers]
     pre_dev = torch.tensor([tokens - 1], dtype=torch.int32, device=device)
 
-    copy_out = torch.cuda.Stream(device)
-    ev_out = [torch.cuda.Event() for _ in range(LAYERS)]
+    dev_out = torch.empty(LAYERS, HEADS * DIM, dtype=torch.bfloat16, device=device)
 
     def e2e_step():
-        # one H2D of the step's q/k/v, then the 16 layers back to back on the
-        # main stream (nothing waits between them, so each launch still
-        # overlaps its predecessor's tail); each layer's output leaves by its
-        # own D2H on a copy stream, overlapping the later layers, and the
-        # step ends when the last D2H has landed
-        main = torch.cuda.current_stream(device)
         dev_in.copy_(host_in, non_blocking=True)
-        copy_out.wait_stream(main)
-        for l in range(LAYERS):
-            o = att.attend(dq[l], dk[l], dv[l], layers[l][0], pre_dev, block_table=tables[l])
-            ev_out[l].record(main)
-            with torch.cuda.stream(copy_out):
-                copy_out.wait_event(ev_out[l])
-                host_out[l].copy_(o.view(-1), non_blocking=True)
-        main.wait_stream(copy_out)
+        outs = [att.attend(dq[l], dk[l], dv[l], layers[l][0], pre_dev, block_table=tables[l]).view(1, -1)
+                for l in range(LAYERS)]
+        # the 16 outputs (the adapter's persistent buffers) gathered on the
+        # device, then one D2H of the step's result
+        torch.cat(outs, dim=0, out=dev_out)
+        host_out.copy_(dev_out, non_blocking=True)
 
     e2e_graph = capture(e2e_step, args.warmup)
     for _ in range(args.warmup):
@@ -574,8 +564,8 @@ def run_single(args, device) -> dict:
             "d2h_bytes_per_step": d2h,
             "api": ("qwarz_b200.attention.attend per layer (the drop-in boundary: validation, "
                     "persistent output, append + split + combine), inside the caller's CUDA graph; "
-                    "one pinned H2D of the step's q/k/v; per layer one D2H of its output on a copy "
-                    "stream that overlaps the later layers' kernels"),
+                    "one pinned H2D of the step's q/k/v; the 16 outputs gathered on the device "
+                    "(torch.cat) and one D2H"),
             "eager_us_per_step": eager_ms * 1e3,
             "eager_note": "the same 16 attend() calls and copies without a graph (host-bound Python dispatch)",
         },
@@ -679,23 +669,12 @@ def run_sharded(args, rank: int, world: int, device) -> dict | None:
     dv = [dev_in[l, HEADS * DIM + KV_HEADS * DIM:].view(1, 1, KV_HEADS, DIM) for l in range(LAYERS)]
     do = [dev_out[l].view(1, 1, HEADS, DIM) for l in range(LAYERS)]
 
-    copy_out = torch.cuda.Stream(device)
-    ev_out = [torch.cuda.Event() for _ in range(LAYERS)]
-
     def e2e_step():
-        # one H2D of the step's q/k/v; each layer's output leaves by its own
-        # D2H on a copy stream that overlaps the later layers' kernels
-        main = torch.cuda.current_stream(device)
         dev_in.copy_(host_in, non_blocking=True)
-        copy_out.wait_stream(main)
         for l in range(LAYERS):
             cache, perm = layers[l]
             dec.step(dq[l], dk[l], dv[l], cache, perm, pre, do[l])
-            ev_out[l].record(main)
-            with torch.cuda.stream(copy_out):
-                copy_out.wait_event(ev_out[l])
-                host_out[l].copy_(dev_out[l], non_blocking=True)
-        main.wait_stream(copy_out)
+        host_out.copy_(dev_out, non_blocking=True)
 
     e2e_graph = capture(e2e_step, args.warmup)
     e2e_ms = timed(e2e_graph, True)
@@ -805,8 +784,8 @@ def run_sharded(args, rank: int, world: int, device) -> dict | None:
             "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
             "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
             "api": f"qwarz_b200.sharded.ShardedDecode.step per layer ({exchange} exchange inside); one "
-                   "pinned H2D of the step's q/k/v per rank, per layer one D2H of its output on a copy "
-                   "stream that overlaps the later layers' kernels; one CUDA graph, max over ranks",
+                   "pinned H2D of the step's q/k/v and one D2H of its outputs per rank; one CUDA graph, "
+                   "max over ranks",
         },
         "gpu_launches": args.steps * LAYERS * (2 if exchange == "peer" else 4),
         "clocks": clocks.summary(),

@@ -33,14 +33,16 @@ __global__ void __launch_bounds__(256) lse_combine_kernel(const CombineParams p)
   __shared__ float red_m[GROUPS];
   const int row = blockIdx.x;
   const int tid = threadIdx.x, grp = tid >> 5, lane = tid & 31;
-  griddep_wait();               // the partials come from the previous kernel
-  griddep_launch_dependents();  // the next kernel may begin its launch
   constexpr int kRotPitch = 33;
   __shared__ float rot_h[MODE == kCombineRotate ? 32 * kRotPitch : 1];
   __shared__ float rot_v[MODE == kCombineRotate ? kHeadDim : 1];
   if constexpr (MODE == kCombineRotate) {
+    // the rotation is a constant input, not written by the split kernel: it
+    // is read while the split drains
     for (int k = tid; k < 1024; k += 256) rot_h[(k >> 5) * kRotPitch + (k & 31)] = __ldg(p.h32 + k);
   }
+  griddep_wait();               // the partials come from the previous kernel
+  griddep_launch_dependents();  // the next kernel may begin its launch
   const float* ml = p.pml + (long long)row * p.ml_row;
   const float* po = p.po + (long long)row * p.o_row + lane * 8;
   const int S = p.num_splits;
