@@ -1,7 +1,7 @@
 """Benchmark of the NVFP4-KV decode attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c3|c4|c5|prefill|all|profile_*]
+                    [--workload auto|c3|c4|c5|k8v4|prefill|all|profile_*]
 
 Default workload ("auto"):
 
@@ -10,8 +10,10 @@ N = 1   BASELINE config 2.  One step is q_len 1 decode attention over 16
         tokens.  The line also carries sub-records of the other single-GPU
         configs: the MTP7 verify at 32,768 and 131,072 tokens beside the
         decode at the same contexts (config 3), 262,144 tokens on one GPU
-        (config 4) and the FP8 draft, six steps in one CUDA graph, at the 16
-        chunks the config names (config 5).
+        (config 4), the FP8 draft, six steps in one CUDA graph, at the 16
+        chunks the config names (config 5), the K8/V4 slot (decode at 65,536
+        tokens, verify at 32,768 and 131,072) and the two prefill kernels
+        (NVFP4 pages and the draft model's FP16 rows).
 N > 1   BASELINE config 4, strong scaling.  16 layers of one 262,144-token
         sequence, its 1,024 pages split contiguously over the N GPUs.  Per
         layer every rank runs the shard split (the rank whose pages hold the
@@ -586,6 +588,7 @@ def run_single(args, device) -> dict:
         extras["c4_262144_one_gpu"] = nvfp4_config(ops, device, stream, args, pk, C4_TOKENS, 4)["q1"]
         extras["c5_draft_fp8"] = c5_record(device, stream, args, pk)
         extras["k8v4"] = k8v4_record(device, stream, args, pk)
+        extras["prefill"] = prefill_record(ops, device, stream, args, pk)
         result["configs"] = extras
     return result
 
@@ -793,6 +796,101 @@ def run_sharded(args, rank: int, world: int, device) -> dict | None:
 
 
 # ------------------------------------------------- other BASELINE configs
+def prefill_record(ops, device, stream, args, pk):
+    """The prefill kernels: the NVFP4 prefill (one launch over the pages)
+    against the 8-row-window route through the verify kernel it replaces,
+    and the draft-model prefill (FP16 K/V read in place) against the
+    reference's torch SDPA route for the same shapes, each at 8,192 new rows
+    onto an empty cache and 4,096 onto 61,440."""
+    res = {}
+    g = torch.Generator(device=device).manual_seed(7)
+    dtype = torch.bfloat16
+    # NVFP4 prefill: one launch over the pages vs the 8-row-window route
+    # through the verify kernel it replaces
+    for pre, S in ((0, 8192), (61440, 4096)):
+        tokens = pre + S
+        pages = (tokens + PAGE - 1) // PAGE
+        c, perm = build_layer(ops, device, pages, tokens, seed=5000 + S)
+        q = torch.randn(S, HEADS, DIM, generator=g, device=device).to(dtype)
+        out = torch.empty_like(q)
+        pre_t = torch.tensor([pre], dtype=torch.int32, device=device)
+
+        def prefill():
+            ops.nvfp4_prefill(q, c[0], c[1], c[2], c[3], perm, pre_t, out)
+
+        splits = ops.default_splits(device, tokens, 8)
+        po, pml = ops.split_workspace(device, 8, splits)
+        wl = torch.arange(pre, pre + S, 8, dtype=torch.int32, device=device)
+
+        def windows():
+            for w in range(S // 8):
+                ops.attn_split(q[8 * w:8 * w + 8], c[0], c[1], perm, wl[w:w + 1], po, pml, c[2], c[3], splits)
+                ops.attn_combine(po, pml, out[8 * w:8 * w + 8], splits)
+
+        for _ in range(2):
+            prefill()
+        ms = cuda_time(prefill, 5, stream) / 5
+        ms_w = graph_ms(windows, 1, 2, stream)  # the old route, graph-captured
+        flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
+        res[f"prefill_{pre}+{S}"] = {
+            "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+            "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
+            "windowed_verify_us": ms_w * 1e3, "speedup_vs_windows": ms_w / ms}
+        del c, perm
+        torch.cuda.empty_cache()
+    # draft-model prefill: FP16 K/V read in place vs the reference's torch
+    # route for the same shapes (draft.py:33-86: SDPA causal when S == T,
+    # else the LSE merge of two flash calls)
+    for pre, S in ((0, 8192), (61440, 4096)):
+        T = pre + S
+        qd = torch.randn(1, S, HEADS, DIM, generator=g, device=device).half()
+        kd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
+        vd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
+        outd = torch.empty_like(qd)
+
+        def ours():
+            ops.draft_prefill(qd, kd, vd, outd, DIM ** -0.5)
+
+        expand = [False]  # GQA through the flash op, else heads repeated first
+
+        def sdpa_route():
+            qt, kt, vt = qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2)
+            if pre == 0:
+                o = torch.nn.functional.scaled_dot_product_attention(
+                    qt, kt, vt, is_causal=True, scale=DIM ** -0.5, enable_gqa=True)
+            else:
+                if expand[0]:
+                    kt = kt.repeat_interleave(HEADS // KV_HEADS, 1)
+                    vt = vt.repeat_interleave(HEADS // KV_HEADS, 1)
+                op = torch.ops.aten._scaled_dot_product_flash_attention
+                o1, l1, *_ = op(qt, kt[:, :, :pre], vt[:, :, :pre], 0.0, False, False, scale=DIM ** -0.5)
+                o2, l2, *_ = op(qt, kt[:, :, pre:], vt[:, :, pre:], 0.0, True, False, scale=DIM ** -0.5)
+                a, b = l1.unsqueeze(-1), l2.unsqueeze(-1)
+                tot = torch.logaddexp(a, b)
+                o = (o1.float() * (a - tot).exp() + o2.float() * (b - tot).exp()).half()
+            return o.transpose(1, 2).contiguous()
+
+        for _ in range(2):
+            ours()
+        ms = cuda_time(ours, 5, stream) / 5
+        try:
+            sdpa_route()
+        except RuntimeError:
+            expand[0] = True
+        for _ in range(2):
+            sdpa_route()
+        ms_ref = cuda_time(sdpa_route, 3, stream) / 3
+        flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
+        res[f"draft_prefill_{pre}+{S}"] = {
+            "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
+            "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
+            "torch_sdpa_route_us": ms_ref * 1e3, "sdpa_heads_repeated": expand[0],
+            "speedup_vs_sdpa_route": ms_ref / ms}
+        del qd, kd, vd, outd
+        torch.cuda.empty_cache()
+    return res
+
+
 def run_extra(args, device) -> dict:
     """--workload c3|c4|c5|prefill|all: the other configs on one GPU, one
     JSON object (not the driver's headline line)."""
@@ -807,89 +905,7 @@ def run_extra(args, device) -> dict:
     if args.workload in ("c3", "all"):
         res["configs"]["c3_verify"] = c3_record(ops, device, stream, args, pk)
     if args.workload in ("prefill", "all"):
-        # NVFP4 prefill: one launch over the pages vs the 8-row-window route
-        # through the verify kernel it replaces
-        for pre, S in ((0, 8192), (61440, 4096)):
-            tokens = pre + S
-            pages = (tokens + PAGE - 1) // PAGE
-            c, perm = build_layer(ops, device, pages, tokens, seed=5000 + S)
-            q = torch.randn(S, HEADS, DIM, generator=g, device=device).to(dtype)
-            out = torch.empty_like(q)
-            pre_t = torch.tensor([pre], dtype=torch.int32, device=device)
-
-            def prefill():
-                ops.nvfp4_prefill(q, c[0], c[1], c[2], c[3], perm, pre_t, out)
-
-            splits = ops.default_splits(device, tokens, 8)
-            po, pml = ops.split_workspace(device, 8, splits)
-            wl = torch.arange(pre, pre + S, 8, dtype=torch.int32, device=device)
-
-            def windows():
-                for w in range(S // 8):
-                    ops.attn_split(q[8 * w:8 * w + 8], c[0], c[1], perm, wl[w:w + 1], po, pml, c[2], c[3], splits)
-                    ops.attn_combine(po, pml, out[8 * w:8 * w + 8], splits)
-
-            for _ in range(2):
-                prefill()
-            ms = cuda_time(prefill, 5, stream) / 5
-            ms_w = graph_ms(windows, 1, 2, stream)  # the old route, graph-captured
-            flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
-            res["configs"][f"prefill_{pre}+{S}"] = {
-                "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
-                "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
-                "windowed_verify_us": ms_w * 1e3, "speedup_vs_windows": ms_w / ms}
-            del c, perm
-            torch.cuda.empty_cache()
-        # draft-model prefill: FP16 K/V read in place vs the reference's torch
-        # route for the same shapes (draft.py:33-86: SDPA causal when S == T,
-        # else the LSE merge of two flash calls)
-        for pre, S in ((0, 8192), (61440, 4096)):
-            T = pre + S
-            qd = torch.randn(1, S, HEADS, DIM, generator=g, device=device).half()
-            kd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
-            vd = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).half()
-            outd = torch.empty_like(qd)
-
-            def ours():
-                ops.draft_prefill(qd, kd, vd, outd, DIM ** -0.5)
-
-            expand = [False]  # GQA through the flash op, else heads repeated first
-
-            def sdpa_route():
-                qt, kt, vt = qd.transpose(1, 2), kd.transpose(1, 2), vd.transpose(1, 2)
-                if pre == 0:
-                    o = torch.nn.functional.scaled_dot_product_attention(
-                        qt, kt, vt, is_causal=True, scale=DIM ** -0.5, enable_gqa=True)
-                else:
-                    if expand[0]:
-                        kt = kt.repeat_interleave(HEADS // KV_HEADS, 1)
-                        vt = vt.repeat_interleave(HEADS // KV_HEADS, 1)
-                    op = torch.ops.aten._scaled_dot_product_flash_attention
-                    o1, l1, *_ = op(qt, kt[:, :, :pre], vt[:, :, :pre], 0.0, False, False, scale=DIM ** -0.5)
-                    o2, l2, *_ = op(qt, kt[:, :, pre:], vt[:, :, pre:], 0.0, True, False, scale=DIM ** -0.5)
-                    a, b = l1.unsqueeze(-1), l2.unsqueeze(-1)
-                    tot = torch.logaddexp(a, b)
-                    o = (o1.float() * (a - tot).exp() + o2.float() * (b - tot).exp()).half()
-                return o.transpose(1, 2).contiguous()
-
-            for _ in range(2):
-                ours()
-            ms = cuda_time(ours, 5, stream) / 5
-            try:
-                sdpa_route()
-            except RuntimeError:
-                expand[0] = True
-            for _ in range(2):
-                sdpa_route()
-            ms_ref = cuda_time(sdpa_route, 3, stream) / 3
-            flops = 4 * HEADS * DIM * sum(pre + s + 1 for s in range(S))
-            res["configs"][f"draft_prefill_{pre}+{S}"] = {
-                "pre": pre, "q_len": S, "us_per_layer": ms * 1e3, "TFLOPs": flops / (ms * 1e-3) / 1e12,
-                "tensor_frac_of_measured_bf16": flops / (ms * 1e-3) / 1e12 / pk.get("bf16_tflops", 1590.0),
-                "torch_sdpa_route_us": ms_ref * 1e3, "sdpa_heads_repeated": expand[0],
-                "speedup_vs_sdpa_route": ms_ref / ms}
-            del qd, kd, vd, outd
-            torch.cuda.empty_cache()
+        res["configs"].update(prefill_record(ops, device, stream, args, pk))
     if args.workload in ("c4", "all"):
         res["configs"]["c4_262144_one_gpu"] = nvfp4_config(ops, device, stream, args, pk, C4_TOKENS, 4)["q1"]
     if args.workload in ("c5", "all"):

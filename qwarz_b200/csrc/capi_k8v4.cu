@@ -134,6 +134,8 @@ int qwz_k8v4_combine(const float* partial_o, const float* partial_ml, void* out,
 int qwz_k8v4_gather(const void* words, const void* scales, const int32_t* block_table, int32_t table_width,
                     int32_t num_pages, int32_t length, int32_t bits, void* out, void* stream) {
   if (!words || !scales || !block_table || !out) return fail(QWZ_EINVAL, "words, scales, block_table and out are required");
+  if (!aligned(words, 4) || !aligned(scales, 2) || !aligned(out, 2))
+    return fail(QWZ_EINVAL, "words must be 4-byte aligned, scales and out 2-byte aligned");
   if (bits != 4 && bits != 8) return fail(QWZ_EINVAL, "bits must be 8 (K) or 4 (V)");
   if (table_width <= 0 || num_pages <= 0 || length < 0) return fail(QWZ_EINVAL, "bad table width, pool or length");
   if ((long long)length > (long long)table_width * qwz::kPage)

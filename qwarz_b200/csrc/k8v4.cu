@@ -183,11 +183,9 @@ __global__ void __launch_bounds__(512) k8v4_append_kernel(K8v4AppendParams p) {
   if (pp < 0) return;
   const long long row = (long long)pp * kPage + (pos & (kPage - 1));
   const T* src = reinterpret_cast<const T*>(is_v ? p.v : p.k) + ((size_t)s * kKvHeads + h) * kHeadDim + j * kBlock;
-  float x;
-  if constexpr (sizeof(T) == 2) {
-    const unsigned short bits = reinterpret_cast<const unsigned short*>(src)[lane];
-    x = InTraits<T>::to_float2((uint32_t)bits).x;
-  }
+  static_assert(sizeof(T) == 2, "FP16 or BF16 rows");
+  const unsigned short raw = reinterpret_cast<const unsigned short*>(src)[lane];
+  float x = InTraits<T>::to_float2((uint32_t)raw).x;
 #pragma unroll
   for (int st = 1; st < kBlock; st <<= 1) {
     const float o = __shfl_xor_sync(0xffffffffu, x, st);
