@@ -36,6 +36,13 @@ DECODE_POLICY = {
     "draft": {"kernel": "fp8_draft_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
               "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37},
     "combine": {"kernel": "lse_combine_kernel", "threads": 256, "split_groups": 8},
+    "k8v4_q1": {"kernel": "k8v4_decode16_kernel", "warps": 17,
+                "roles": "two groups of 8 (even / odd 128-token stages), one TMA producer",
+                "stage_tokens": 128, "stages": 4, "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
+                "dequant": "bit planes -> FP16 by rotate/merge and fma.rn.f16x2", "ctas_per_sm": 1},
+    "k8v4_q2-8": {"kernel": "k8v4_split_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
+                  "mma": "mma.sync m16n8k16, S^T = K Q^T per 16 tokens, O^T = V^T P^T per 32-dim block"},
+    "k8v4_combine": {"kernel": "lse_combine_kernel (rotate mode)", "threads": 256, "out": "R^T O per 32 dims"},
 }
 
 
@@ -62,6 +69,23 @@ def call_split(packed, q_len: int, num_pages: int, sm_scale: float, dtype: int, 
     lib = _lib.load()
     _lib.check(lib.qwz_attn_split(*values, q_len, num_pages, float(sm_scale), dtype, stream),
                "qwz_attn_split")
+
+
+def call_k8v4_split(packed, q_len: int, num_pages: int, sm_scale: float, dtype: int, stream: int) -> None:
+    """Invoke qwz_k8v4_split (the K8/V4 slot: same 15 + 2 order, h32 given,
+    sinks NULL) with a `pack_split_args` list."""
+    if [n for n, _, _ in packed] != list(SPLIT_ARG_NAMES + TRAILING_ARG_NAMES):
+        raise ValueError("packed arguments are not in ABI order")
+    values = [v if k == "int32" else (v or None) for _, k, v in packed]
+    lib = _lib.load()
+    _lib.check(lib.qwz_k8v4_split(*values, q_len, num_pages, float(sm_scale), dtype, stream), "qwz_k8v4_split")
+
+
+def call_k8v4_combine(partial_o: int, partial_ml: int, out: int, h32: int, num_splits: int, q_len: int,
+                      dtype: int, stream: int) -> None:
+    lib = _lib.load()
+    _lib.check(lib.qwz_k8v4_combine(partial_o, partial_ml, out, h32, num_splits, None, q_len, dtype, stream),
+               "qwz_k8v4_combine")
 
 
 def call_combine(partial_o: int, partial_ml: int, out: int, num_splits: int, q_len: int,

@@ -299,3 +299,45 @@ def test_graph_patch_of_k8v4_split_and_combine_nodes(cuda):
         assert torch.equal(out, eager(table[:width], lens, splits, split_len)), (splits, split_len, exec_too)
     assert _lib.device_error(clear=True) == 0
     del g
+
+
+@pytest.mark.parametrize("q_len,split_len,splits", [(1, 0, 20), (1, 512, 8), (7, 0, 11), (7, 1024, 3)])
+def test_k8v4_slot_called_with_packed_arguments(cuda, q_len, split_len, splits):
+    """The slot as the reference's kernel wrapper calls it: the 15 + 2
+    arguments in ABI order (tests/test_attention_kernel_abi.py:16-20, int32 at
+    11, 12, 13), h32 in slot 10, then the 6-argument combine; equal to the
+    torch wrappers' launch and within the gate of the oracle."""
+    from qwarz_b200 import _lib, k8v4, ops
+    from qwarz_b200.contract import backend
+
+    P, pre = 12, 2900
+    table = rng.permutation(97, P)
+    kt = torch.from_numpy(cases.kv_rows(98, pre + q_len, 4)).half()
+    vt = torch.from_numpy(cases.kv_rows(99, pre + q_len, 4)).half()
+    c = ok8.empty_cache(P)
+    ok8.write_rows(c, kt.float().numpy(), vt.float().numpy(), table, 0)
+    dev = _dev_cache(c, cuda)
+    q = torch.from_numpy(rng.normal(96 + q_len, q_len * 24 * 256).astype(np.float32).reshape(q_len, 24, 256)).half().to(cuda)
+    h32 = k8v4.hadamard32(cuda)
+    t = torch.from_numpy(table).to(cuda)
+    lens = torch.tensor([pre], dtype=torch.int32, device=cuda)
+    po, pml = ops.split_workspace(cuda, q_len, splits)
+    out = torch.empty_like(q)
+    ptrs = {"q": q.data_ptr(), "k_cache": dev[0].data_ptr(), "v_cache": dev[1].data_ptr(),
+            "block_table": t.data_ptr(), "cache_seqlens": lens.data_ptr(), "out": out.data_ptr(),
+            "partial_o": po.data_ptr(), "partial_ml": pml.data_ptr(), "k_scales": dev[2].data_ptr(),
+            "v_scales": dev[3].data_ptr(), "h32": h32.data_ptr()}
+    packed = backend.pack_split_args(ptrs, {"split_len": split_len, "num_pages_per_seq": P, "num_splits": splits})
+    stream = torch.cuda.current_stream().cuda_stream
+    backend.call_k8v4_split(packed, q_len, P, 1 / 16, _lib.DTYPE_F16, stream)
+    backend.call_k8v4_combine(po.data_ptr(), pml.data_ptr(), out.data_ptr(), h32.data_ptr(), splits, q_len,
+                              _lib.DTYPE_F16, stream)
+    po2, pml2 = ops.split_workspace(cuda, q_len, splits)
+    out2 = torch.empty_like(q)
+    k8v4.split(q, dev, t, lens, po2, pml2, h32, splits, split_len)
+    k8v4.combine(po2, pml2, out2, h32, splits)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+    assert _lib.device_error(clear=True) == 0
+    ref = ok8.attention(q.cpu(), c, table, pre)
+    assert_close_rotated(out.float().cpu().numpy(), ref.numpy(), f"packed k8v4 q_len={q_len}")
