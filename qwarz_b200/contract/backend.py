@@ -28,7 +28,7 @@ DECODE_POLICY = {
     "q1": {"kernel": "nvfp4_decode_kernel", "warps": 8, "stage_tokens": 256, "stages": 3,
            "copy": "TMA 2-D boxes, 128-byte swizzle", "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
            "ctas_per_sm": 1, "append": "fused when called through qwz_nvfp4_attend"},
-    "q2-8": {"kernel": "nvfp4_verify_tc_kernel", "warps": 19,
+    "q2-8": {"kernel": "verify_tc_kernel<VtNvfp4>", "warps": 19,
              "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
              "stage_tokens": 128, "stages": {"K": 3, "V": 2}, "copy": "TMA 2-D boxes, 128-byte swizzle",
              "mma": "tcgen05 kind::f16 M=128: S^T = K Q^T (K from TMEM, N=16/32/48), O^T = V^T P^T (FP16 P)",
@@ -40,8 +40,11 @@ DECODE_POLICY = {
                 "roles": "two groups of 8 (even / odd 128-token stages), one TMA producer",
                 "stage_tokens": 128, "stages": 4, "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
                 "dequant": "bit planes -> FP16 by rotate/merge and fma.rn.f16x2", "ctas_per_sm": 1},
-    "k8v4_q2-8": {"kernel": "k8v4_split_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
-                  "mma": "mma.sync m16n8k16, S^T = K Q^T per 16 tokens, O^T = V^T P^T per 32-dim block"},
+    "k8v4_q2-8": {"kernel": "verify_tc_kernel<VtK8v4>", "warps": 19,
+                  "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
+                  "stage_tokens": 128, "stages": {"K": 2, "V": 2},
+                  "dequant": "8x8 bit transpose per (token, 32-dim block), fma.rn.f16x2",
+                  "mma": "tcgen05 kind::f16 M=128 as the NVFP4 verify"},
     "k8v4_combine": {"kernel": "lse_combine_kernel (rotate mode)", "threads": 256, "out": "R^T O per 32 dims"},
 }
 

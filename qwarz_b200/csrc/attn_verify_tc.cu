@@ -62,11 +62,11 @@ constexpr int kVtPidCache = 512;
 constexpr uint32_t kTmK = 0, kTmS = 128, kTmO = 256;
 constexpr uint32_t kTmCols = 512;
 
-template <int N>
+template <int N, class F>
 struct VtLayout {
-  static constexpr int kKRing = 0;                                   // 3 x 18 KB
-  static constexpr int kVRing = kKRing + kVtKStages * kVtHalfStage;  // 2 x 18 KB
-  static constexpr int kVf = 92160;                                  // V FP16: [2h+a][128 tok][128 B]
+  static constexpr int kKRing = 0;                                      // K tiles (NVFP4: 3 x 18 KB)
+  static constexpr int kVRing = kKRing + F::kKStages * F::kKStage;      // V tiles (NVFP4: 2 x 18 KB)
+  static constexpr int kVf = (kVRing + F::kVStages * F::kVStage + 1023) / 1024 * 1024;  // V FP16: [2h+a][128 tok][128 B]
   static constexpr int kQ = kVf + 4 * 16384;                         // Q: 4 k-atoms [N x 128 B]
   static constexpr int kPAtoms = (N + 63) / 64;                      // P: n-atoms [128 tok][128 B]
   static constexpr int kP = kQ + N * 512;
@@ -79,9 +79,9 @@ struct VtLayout {
   static constexpr int kWred = kMref + 4 * N;                        // [parts][4 q][N / parts]
   static constexpr int kPid = kWred + 4 * 4 * N;
   static constexpr int kBytes = kPid + 4 * kVtPidCache + 1024;
-  static_assert(kVRing + kVtVStages * kVtHalfStage <= kVf && kVf % 1024 == 0, "ring / V layout");
+  static_assert(kVRing + F::kVStages * F::kVStage <= kVf && kVf % 1024 == 0, "ring / V layout");
   static_assert(kQ % 1024 == 0 && kP % 1024 == 0 && kBars % 1024 == 0, "operand atoms are 1024-byte aligned");
-  static_assert(8 * (2 * kVtKStages + 2 * kVtVStages + 5) <= 128 && (kMeta + 24) % 8 == 0,
+  static_assert(8 * (2 * F::kKStages + 2 * F::kVStages + 5) <= 128 && (kMeta + 24) % 8 == 0,
                 "mbarriers are 8-byte aligned");
   static_assert(kRowfac % 16 == 0, "row factors are read as float4");
 };
@@ -280,21 +280,48 @@ QWZ_DEVINL void sts64(uint32_t addr, uint32_t a, uint32_t b) {
 
 }  // namespace
 
-template <typename T, int N>
+// The NVFP4 cache: a K or V tile is one 128-token box of E2M1 codes (128 B
+// a row, 128-byte swizzle) and one of E4M3 scales (16 B a row).
+struct VtNvfp4 {
+  static constexpr int kKStages = kVtKStages, kVStages = kVtVStages;
+  static constexpr int kKStage = kVtHalfStage, kVStage = kVtHalfStage;
+  static constexpr bool kRotated = false;
+  QWZ_DEVINL static void issue(bool is_k, const SplitParams& p, uint32_t dst, int kvh, int y, uint32_t bar) {
+    tma_load_2d(dst, is_k ? &p.tm_kc : &p.tm_vc, kvh * kCodeBytes, y, bar);
+    tma_load_2d(dst + kVtCodeBox, is_k ? &p.tm_ks : &p.tm_vs, kvh * kScaleBytes, y, bar);
+  }
+  template <class Put>
+  QWZ_DEVINL static void dequant_k(uint32_t st, int tt, int u, Put put) {
+    dequant_row_part(st, st + kVtCodeBox, tt, u, false, put);
+  }
+  template <class Put>
+  QWZ_DEVINL static void dequant_v(uint32_t st, int tt, int u, bool zero, Put put) {
+    dequant_row_part(st, st + kVtCodeBox, tt, u, zero, put);
+  }
+  template <typename T, int N>
+  QWZ_DEVINL static void stage(const SplitParams& p, int kvh, uint32_t qbase, float* rowfac, bool, int mw,
+                               int lane) {
+    stage_q<T, N>(p, kvh, qbase, rowfac, mw, lane);
+  }
+  QWZ_DEVINL static bool rotation_check(const SplitParams&, int) { return true; }
+  QWZ_DEVINL static int o_dim(int d) { return d; }  // the V tile's d order is the head's
+};
+
+template <typename T, int N, class F>
 __global__ void __launch_bounds__(kVtWarps * 32, 1)
-    nvfp4_verify_tc_kernel(const __grid_constant__ SplitParams p) {
-  using L = VtLayout<N>;
+    verify_tc_kernel(const __grid_constant__ SplitParams p) {
+  using L = VtLayout<N, F>;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sraw = smem_u32(smem);
   const uint32_t sb = (sraw + 1023u) & ~1023u;
   uint8_t* sg = smem + (sb - sraw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y;
-  const uint32_t bar_kfull = sb + L::kBars, bar_kempty = bar_kfull + 8 * kVtKStages;
-  const uint32_t bar_vfull = bar_kempty + 8 * kVtKStages, bar_vempty = bar_vfull + 8 * kVtVStages;
-  const uint32_t bar_kready = bar_vempty + 8 * kVtVStages, bar_pv = bar_kready + 8;
+  const uint32_t bar_kfull = sb + L::kBars, bar_kempty = bar_kfull + 8 * F::kKStages;
+  const uint32_t bar_vfull = bar_kempty + 8 * F::kKStages, bar_vempty = bar_vfull + 8 * F::kVStages;
+  const uint32_t bar_kready = bar_vempty + 8 * F::kVStages, bar_pv = bar_kready + 8;
   const uint32_t bar_s = bar_pv + 8, bar_o = bar_s + 16;  // bar_s: one per S buffer
-  int* kstage_end = reinterpret_cast<int*>(sg + L::kMeta);  // [kVtKStages]
+  int* kstage_end = reinterpret_cast<int*>(sg + L::kMeta);  // [F::kKStages]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sg + L::kMeta + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sg + L::kMeta + 20);
   const uint32_t bar_fin = sb + L::kMeta + 24;  // the MMA thread's last commit
@@ -306,12 +333,12 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
 
   if (tid == 0) {
 #pragma unroll
-    for (int s = 0; s < kVtKStages; ++s) {
+    for (int s = 0; s < F::kKStages; ++s) {
       mbar_init(bar_kfull + 8 * s, 1);
       mbar_init(bar_kempty + 8 * s, kVtMathWarps);
     }
 #pragma unroll
-    for (int s = 0; s < kVtVStages; ++s) {
+    for (int s = 0; s < F::kVStages; ++s) {
       mbar_init(bar_vfull + 8 * s, 1);
       mbar_init(bar_vempty + 8 * s, kVtMathWarps);
     }
@@ -338,8 +365,9 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     for (int i = lane; i < min(rg.n_st, kVtPidCache); i += 32)
       pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
   }
+  const bool had = F::rotation_check(p, tid);  // the K8/V4 rotation test (a CTA-wide barrier)
   if (warp >= kVtMath0) {
-    stage_q<T, N>(p, kvh, sb + L::kQ, rowfac, warp - kVtMath0, lane);
+    F::template stage<T, N>(p, kvh, sb + L::kQ, rowfac, had, warp - kVtMath0, lane);
     fence_proxy_async_smem();  // Q is read by the tensor core
   }
   tc::fence_before();
@@ -350,7 +378,8 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   if (warp == 0 || warp == 2) {
     // ----------------------------------------------- producers (K: 0, V: 2)
     const bool is_k = warp == 0;
-    const int nst = is_k ? kVtKStages : kVtVStages;
+    const int nst = is_k ? F::kKStages : F::kVStages;
+    const int stage_bytes = is_k ? F::kKStage : F::kVStage;
     const uint32_t ring = sb + (is_k ? L::kKRing : L::kVRing);
     const uint32_t full = is_k ? bar_kfull : bar_vfull, empty = is_k ? bar_kempty : bar_vempty;
     const CUtensorMap* tm_c = is_k ? &p.tm_kc : &p.tm_vc;
@@ -377,11 +406,10 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
           mbar_arrive(fb);
           continue;
         }
-        mbar_arrive_expect_tx(fb, kVtHalfStage);
-        const uint32_t dst = ring + s * kVtHalfStage;
+        mbar_arrive_expect_tx(fb, stage_bytes);
+        const uint32_t dst = ring + s * stage_bytes;
         const int y = pp * kPage + kVtTile * (i & 1);
-        tma_load_2d(dst, tm_c, kvh * kCodeBytes, y, fb);
-        tma_load_2d(dst + kVtCodeBox, tm_s, kvh * kScaleBytes, y, fb);
+        F::issue(is_k, p, dst, kvh, y, fb);
       }
       // never leave with copies in flight (only reachable after an abort)
       for (int i = max(issued - nst, 0); i < issued; ++i)
@@ -460,12 +488,12 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
     // K(j) -> TMEM, thread = token tt, head-dim part u (columns 16 g ..);
     // returns the tile's valid end, read before the ring slot is released
     auto do_k = [&](int j) -> int {
-      const int s = j % kVtKStages;
-      ok &= mbar_wait(bar_kfull + 8 * s, (j / kVtKStages) & 1);
+      const int s = j % F::kKStages;
+      ok &= mbar_wait(bar_kfull + 8 * s, (j / F::kKStages) & 1);
       const int end = kstage_end[s];
-      const uint32_t st = sb + L::kKRing + s * kVtHalfStage;
+      const uint32_t st = sb + L::kKRing + s * F::kKStage;
       const uint32_t col = tbase + lane_base + kTmK;
-      dequant_row_part(st, st + kVtCodeBox, tt, u, false,
+      F::dequant_k(st, tt, u,
                        [&](int g, const uint32_t (&r)[16]) { tc::st_32x32b_x16(col + 16 * g, r); });
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_kempty + 8 * s);
@@ -567,11 +595,11 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       // ------------------------------ V(i) and P(i) after PV(i-1) is done
       if (i > 0) ok &= mbar_wait(bar_o, (i - 1) & 1);
       {
-        const int s = i % kVtVStages;
-        ok &= mbar_wait(bar_vfull + 8 * s, (i / kVtVStages) & 1);
-        const uint32_t st = sb + L::kVRing + s * kVtHalfStage;
+        const int s = i % F::kVStages;
+        ok &= mbar_wait(bar_vfull + 8 * s, (i / F::kVStages) & 1);
+        const uint32_t st = sb + L::kVRing + s * F::kVStage;
         const uint32_t vrow = sb + L::kVf + tt * 128;
-        dequant_row_part(st, st + kVtCodeBox, tt, u, t0 + tt >= vend, [&](int g, const uint32_t (&r)[16]) {
+        F::dequant_v(st, tt, u, t0 + tt >= vend, [&](int g, const uint32_t (&r)[16]) {
           // d = 32g + 8j .. +7: atom g / 2 (64 d), 16-byte chunk 4 (g % 2) + j of the row
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -629,7 +657,7 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       p.partial_ml[base * 2 + 1] = l;
     }
     {
-      const int d = 128 * ohalf + tt;  // O^T lane tt of M half ohalf
+      const int d = F::o_dim(128 * ohalf + tt);  // O^T lane tt of M half ohalf
       float o[NO];
       if (have_o) {
         ld_cols<NO>(tbase + lane_base + kTmO + N * ohalf + ocol, o);
@@ -656,23 +684,23 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   }
 }
 
-template <typename T, int N>
+template <typename T, int N, class F>
 cudaError_t launch_verify_tc_n(const SplitParams& p, cudaStream_t stream) {
-  using L = VtLayout<N>;
+  using L = VtLayout<N, F>;
   static_assert(L::kBytes <= 227 * 1024, "shared memory");
   static_assert(kTmO + 4 * N <= kTmCols && kTmS + 64 + N <= kTmO, "tensor memory columns");
-  auto kernel = nvfp4_verify_tc_kernel<T, N>;
+  auto kernel = verify_tc_kernel<T, N, F>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
   if (e != cudaSuccess) return e;
   return launch_pdl(kernel, dim3(p.num_splits, kKvHeads), dim3(kVtWarps * 32), L::kBytes, stream, p);
 }
 
-template <typename T>
+template <typename T, class F = VtNvfp4>
 cudaError_t launch_verify_tc(const SplitParams& p, cudaStream_t stream) {
   const int rows = kGroup * p.q_len;
-  if (rows <= 16) return launch_verify_tc_n<T, 16>(p, stream);
-  if (rows <= 32) return launch_verify_tc_n<T, 32>(p, stream);
-  if (rows <= 48) return launch_verify_tc_n<T, 48>(p, stream);
+  if (rows <= 16) return launch_verify_tc_n<T, 16, F>(p, stream);
+  if (rows <= 32) return launch_verify_tc_n<T, 32, F>(p, stream);
+  if (rows <= 48) return launch_verify_tc_n<T, 48, F>(p, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -25,24 +25,18 @@ bool is_split_kernel(const void* f) {
   const void* known[] = {
       reinterpret_cast<const void*>(nvfp4_decode_kernel<__half>),
       reinterpret_cast<const void*>(nvfp4_decode_kernel<__nv_bfloat16>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__half, 16>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__half, 32>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__half, 48>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 16>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 32>),
-      reinterpret_cast<const void*>(nvfp4_verify_tc_kernel<__nv_bfloat16, 48>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 1>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 2>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 3>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 4>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 5>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__half, 6>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 1>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 2>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 3>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 4>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 5>),
-      reinterpret_cast<const void*>(k8v4_split_kernel<__nv_bfloat16, 6>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 16, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 32, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 48, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 16, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 32, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 48, VtNvfp4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 16, VtK8v4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 32, VtK8v4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__half, 48, VtK8v4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 16, VtK8v4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 32, VtK8v4>),
+      reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 48, VtK8v4>),
       reinterpret_cast<const void*>(k8v4_decode16_kernel<__half>),
       reinterpret_cast<const void*>(k8v4_decode16_kernel<__nv_bfloat16>),
   };

@@ -16,28 +16,33 @@
 //   x_rot = FP16((FP32(c) - (2^(b-1) - 0.5)) * (FP32(s) / 2^(b-1)))
 // computed here in FP32, where the product is exact, and rounded once.
 //
-// Attention runs in the rotated domain (spec :61): the split kernel rotates
-// the queries with the caller's h32 matrix (FP32 [32, 32], R) and writes
+// Attention runs in the rotated domain (spec :61): the split kernels rotate
+// the queries with the caller's h32 matrix (FP32 [32, 32], R) and write
 // rotated partials; the combine merges them and restores the output with R^T.
 //
-// Split kernel: one CTA per (split, KV head), 8 warps, 128-token stages in a
-// 3-slot TMA ring (K as two 128-byte-swizzled halves, V swizzled, the FP16
-// scales unswizzled; 52 KB a stage).  For each stage:
+// Decode (q_len 1), k8v4_decode16_kernel: one CTA per (split, KV head), two
+// groups of 8 warps take the even and the odd 128-token stages of the split
+// from a 4-slot TMA ring (K as two 128-byte-swizzled halves, V swizzled, the
+// FP16 scales unswizzled; 52 KB a stage) that a producer warp refills.  For
+// each stage a group runs:
 //   QK   warp w takes tokens 16w..16w+15 and every query row of the head
-//        group (rows = 6 q_len, padded to NT * 8): S^T = K Q^T with
-//        mma.sync m16n8k16, the K A-fragments unpacked straight from the bit
-//        planes (a thread's 8 dims of a block sit at bits 2q + {0,1,8,9,16,
-//        17,24,25} of each plane, so one shift and two masked merges per
-//        plane give their codes) and Q B-fragments by ldmatrix;
-//   max  the warps' row maxima meet in shared memory (one barrier), every
+//        group: S^T = K Q^T with mma.sync m16n8k16, the K A-fragments
+//        unpacked straight from the bit planes (a thread's 8 dims q + 4k of a
+//        block come out of the 8 planes with one rotate and one masked merge
+//        per plane) and Q B-fragments by ldmatrix;
+//   max  the group's row maxima meet in shared memory (one barrier), every
 //        warp derives the same running max, P = 2^(S - m) goes to shared
 //        memory in FP16 (second barrier);
 //   PV   warp w owns the 32 dims of block w for all 128 tokens:
 //        O^T[d x rows] += V^T P^T, the V A-fragments unpacked from the 4 bit
-//        planes (bits g + {0, 8, 16, 24}), P^T by ldmatrix.trans.
+//        planes (dims g + 8k), P^T by ldmatrix.trans.
 // The running max and O rescale are per row and need no further exchange,
 // because the PV accumulator's columns are the same rows as the QK
-// accumulator's columns in every thread.
+// accumulator's columns in every thread; the two groups merge at the end.
+//
+// Verify (q_len 2..8): the tcgen05 verify kernel of attn_verify_tc.cu with
+// the VtK8v4 format policy below (whole-block bit transposes by the math
+// threads, Q in the matching dim order).
 
 #include "qwz_common.cuh"
 #include "qwz_kernels.h"
@@ -69,24 +74,6 @@ constexpr int kVBox = kStage * 128;                      // 16 KB
 constexpr int kSBox = kStage * 16;                       // 2 KB: 8 scales of a head
 constexpr int kStageBytes = 2 * kKHalf + kVBox + 2 * kSBox;  // 53,248
 static_assert(kStageBytes % 1024 == 0, "stages stay 1024-byte aligned for the swizzled boxes");
-
-// shared-memory layout of the split kernel (NT n-tiles of 8 query rows)
-template <int NT>
-struct Layout {
-  static constexpr int kRows = NT * 8;
-  static constexpr int kPChunks = NT | 1;                // P^T row: 16-byte chunks (odd: conflict-free)
-  static constexpr int kRing = 0;
-  static constexpr int kQ = kSlots * kStageBytes;        // Q_rot FP16 [rows][256], swizzled chunks
-  static constexpr int kP = kQ + kRows * 512;            // P^T FP16 [128 tok][kPChunks * 8]
-  static constexpr int kH = kP + kStage * kPChunks * 16; // h32 FP32 [32][32]
-  static constexpr int kRed = kH + 4096;                 // row maxima [8 warps][rows]
-  static constexpr int kRedL = kRed + kWarps * kRows * 4;
-  static constexpr int kRowFac = kRedL + kWarps * kRows * 4;  // sm_scale*log2e / row factor
-  static constexpr int kBars = kRowFac + kRows * 4;
-  static constexpr int kStageOk = kBars + 8 * kSlots;
-  static constexpr int kBytes = kStageOk + 4 * kSlots + 1024;  // + alignment slack
-  static_assert(kQ % 1024 == 0 && kP % 16 == 0 && kBars % 8 == 0, "layout alignment");
-};
 
 constexpr float kInvSqrt32 = 0.17677669529663687f;
 
@@ -262,8 +249,8 @@ struct RowState {
   int lim[NT][2];
 };
 
-// A barrier over the warps that share one stage: the whole CTA (bar 0) or a
-// group of 8 warps (named barrier id, 256 threads).
+// A barrier over the 8 warps (256 threads) that share one stage: a named
+// barrier per stage group.
 struct StageBar {
   int id;
   QWZ_DEVINL void sync() const { asm volatile("bar.sync %0, 256;\n" ::"r"(id) : "memory"); }
@@ -388,11 +375,10 @@ QWZ_DEVINL void init_rows(RowState<NT>& rs, const float* rowfac, int q4, int q_l
 // the group): QK, the group's row maxima through red[8 warps][R] (one
 // barrier), P into pbase, the rescale, a second barrier, PV.  Returns false
 // when any thread of the group reports !ok at the first barrier (every
-// thread of the group then returns false).  after_max runs right after the
-// first barrier (the single-group kernel issues its next TMA stage there).
-template <int NT, class AfterMax>
+// thread of the group then returns false).
+template <int NT>
 QWZ_DEVINL bool run_stage(RowState<NT>& rs, uint32_t st, uint32_t qbase, uint32_t pbase, float* red, int t0,
-                          bool sok, bool ok, int warp, int lane, StageBar bar, AfterMax after_max) {
+                          bool sok, bool ok, int warp, int lane, StageBar bar) {
   constexpr int R = NT * 8;
   constexpr int kPRow = (NT | 1) * 16;  // P^T row bytes (odd chunk count: conflict-free ldmatrix)
   const int g = lane >> 2, q4 = lane & 3;
@@ -469,7 +455,6 @@ QWZ_DEVINL bool run_stage(RowState<NT>& rs, uint32_t st, uint32_t qbase, uint32_
     }
   }
   if (bar.any(!ok)) return false;  // every thread of the group leaves together
-  after_max();
 
   // ----------------------------------------- running max, P, rescale
   // P is rounded to FP16 for the PV product; the row sums l add the same
@@ -639,103 +624,6 @@ QWZ_DEVINL void write_partials(const SplitParams& p, const RowState<NT>& rs, con
 
 }  // namespace k8v4
 
-// One CTA per (split, KV head), 8 warps, a 3-slot ring filled by thread 0.
-template <typename T, int NT>
-__global__ void __launch_bounds__(256, 1) k8v4_split_kernel(const __grid_constant__ SplitParams p) {
-  using namespace k8v4;
-  using L = Layout<NT>;
-  constexpr int R = NT * 8;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sb = smem_u32(smem);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q4 = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y;
-  float* red = reinterpret_cast<float*>(smem + L::kRed);
-  float* red_l = reinterpret_cast<float*>(smem + L::kRedL);
-  float* rowfac = reinterpret_cast<float*>(smem + L::kRowFac);
-  int* stage_ok = reinterpret_cast<int*>(smem + L::kStageOk);
-  const uint32_t bars = sb + L::kBars;
-
-  if (tid == 0) {
-    for (int i = 0; i < kSlots; ++i) mbar_init(bars + 8 * i, 1);
-    mbar_fence_init();
-    tma_prefetch_desc(&p.tm_kc);
-    tma_prefetch_desc(&p.tm_vc);
-    tma_prefetch_desc(&p.tm_ks);
-    tma_prefetch_desc(&p.tm_vs);
-  }
-  griddep_wait();  // the length, the table, the cache and q may come from the previous kernel
-  const StageRange rg = stage_range<kStage>(p, split);
-  const int len_all = __ldg(p.seqlens) + p.len_add;
-  __syncthreads();
-
-  // the producer: stage i of this split into ring slot i % 3
-  auto issue = [&](int i) {
-    const int slot = i % kSlots;
-    const uint32_t bar = bars + 8 * slot;
-    const int t0 = p.tok_begin + (rg.st_lo + i) * kStage;
-    const int pp = page_of(p.block_table, p.table_width, p.num_pages, t0);
-    stage_ok[slot] = pp >= 0;
-    if (pp < 0) {
-      mbar_arrive(bar);  // nothing to load: the stage is masked as a whole
-      return;
-    }
-    const int y = pp * kPage + (t0 & (kPage - 1));
-    const uint32_t dst = sb + L::kRing + slot * kStageBytes;
-    mbar_arrive_expect_tx(bar, kStageBytes);
-    tma_load_2d(dst, &p.tm_kc, kvh * 256, y, bar);
-    tma_load_2d(dst + kKHalf, &p.tm_kc, kvh * 256 + 128, y, bar);
-    tma_load_2d(dst + 2 * kKHalf, &p.tm_vc, kvh * 128, y, bar);
-    tma_load_2d(dst + 2 * kKHalf + kVBox, &p.tm_ks, kvh * 16, y, bar);
-    tma_load_2d(dst + 2 * kKHalf + kVBox + kSBox, &p.tm_vs, kvh * 16, y, bar);
-  };
-  int issued = 0;
-  if (tid == 0) {
-    for (; issued < min(2, rg.n_st); ++issued) issue(issued);
-  }
-
-  const bool had = __syncthreads_and(h32_is_hadamard(p.h32, tid, 256)) != 0;
-  stage_q_rot<T>(p, kvh, R, smem + L::kQ, rowfac, had, warp, kWarps, lane);
-  __syncthreads();
-
-  RowState<NT> rs;
-  init_rows<NT>(rs, rowfac, q4, p.q_len, rg.tok_end, len_all);
-  const uint32_t qbase = sb + L::kQ, pbase = sb + L::kP;
-  const StageBar bar{0};
-  bool ok = true;
-  int done = 0;
-  for (int i = 0; i < rg.n_st; ++i) {
-    const int slot = i % kSlots;
-    ok &= mbar_wait(bars + 8 * slot, (i / kSlots) & 1);
-    const int t0 = p.tok_begin + (rg.st_lo + i) * kStage;
-    const bool fine = run_stage<NT>(rs, sb + L::kRing + slot * kStageBytes, qbase, pbase, red, t0,
-                                    stage_ok[slot] != 0, ok, warp, lane, bar, [&] {
-                                      // into the slot stage i-1 used
-                                      if (tid == 0 && issued < rg.n_st) issue(issued++);
-                                    });
-    if (!fine) break;
-    done = i + 1;
-  }
-  griddep_launch_dependents();
-
-  if (!ok || done != rg.n_st) {
-    flag_error(kErrTimeout);
-    // never leave with copies in flight
-    if (tid == 0)
-      for (int i = done; i < issued; ++i)
-        if (!mbar_wait(bars + 8 * (i % kSlots), (i / kSlots) & 1)) break;
-  }
-
-  // -------------------------------------------------------------- epilogue
-  __syncthreads();
-  group_l<NT>(rs, red_l, warp, lane);
-  __syncthreads();
-  float lrow[NT][2];
-  row_totals<NT>(red_l, lane, lrow);
-  write_partials<NT>(p, rs, lrow, ok && done == rg.n_st, split, kvh, warp, lane);
-}
-
 // Decode (q_len 1) with twice the warps: two groups of 8 warps take the
 // even and the odd 128-token stages of the split, each with its own online
 // softmax, from a 4-slot ring that a producer warp (warp 16) refills as a
@@ -861,7 +749,7 @@ __global__ void __launch_bounds__(544, 1) k8v4_decode16_kernel(const __grid_cons
     ok &= mbar_wait(full + 8 * slot, (i / kD16Slots) & 1);
     const int t0 = p.tok_begin + (rg.st_lo + i) * kStage;
     const bool fine = run_stage<1>(rs, sb + L::kRing + slot * kStageBytes, sb + L::kQ, pbase, red, t0,
-                                   stage_ok[slot] != 0, ok, gw, lane, bar, [] {});
+                                   stage_ok[slot] != 0, ok, gw, lane, bar);
     if (!fine) break;
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + 8 * slot);  // this warp is done with the slot
@@ -918,29 +806,198 @@ __global__ void __launch_bounds__(544, 1) k8v4_decode16_kernel(const __grid_cons
   __syncthreads();  // (F)
 }
 
-template <typename T>
-static cudaError_t launch_k8v4_split_t(const SplitParams& p, int nt, cudaStream_t stream) {
-  const dim3 grid(p.num_splits, kKvHeads), block(256);
-#define QWZ_K8_NT(N)                                                                              \
-  case N: {                                                                                       \
-    auto kern = k8v4_split_kernel<T, N>;                                                          \
-    const int smem = k8v4::Layout<N>::kBytes;                                                     \
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    if (e != cudaSuccess) return e;                                                               \
-    return launch_pdl(kern, grid, block, (size_t)smem, stream, p);                                \
+// ------------------------------------------------ tcgen05 verify (q_len 2..8)
+namespace k8v4 {
+
+// 8 x 8 bit transpose of each byte column of 8 plane words (three rounds of
+// block swaps: 4 x 4, 2 x 2, 1 x 1).  Before, bit j of byte m of word i is
+// plane i of dim 8m + j; after, byte m of word j is the code of dim 8m + j.
+QWZ_DEVINL void transpose8(uint32_t (&w)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t t = ((w[i] >> 4) ^ w[i + 4]) & 0x0F0F0F0Fu;
+    w[i + 4] ^= t;
+    w[i] ^= t << 4;
   }
-  switch (nt) {
-    QWZ_K8_NT(1)
-    QWZ_K8_NT(2)
-    QWZ_K8_NT(3)
-    QWZ_K8_NT(4)
-    QWZ_K8_NT(5)
-    QWZ_K8_NT(6)
-    default:
-      return cudaErrorInvalidValue;
+#pragma unroll
+  for (int i = 0; i < 8; i += 4)
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint32_t t = ((w[i + k] >> 2) ^ w[i + k + 2]) & 0x33333333u;
+      w[i + k + 2] ^= t;
+      w[i + k] ^= t << 2;
+    }
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const uint32_t t = ((w[i] >> 1) ^ w[i + 1]) & 0x55555555u;
+    w[i + 1] ^= t;
+    w[i] ^= t << 1;
   }
-#undef QWZ_K8_NT
 }
+
+// K position of dim p of a block in the tile order the verify's unpacking
+// produces (word j of the transpose holds dims j, j + 8, j + 16, j + 24; the
+// f16x2 word 2j + h holds dims j + 16h and j + 16h + 8), and its inverse.
+QWZ_DEVINL int vt_pos(int p) { return 4 * (p & 7) + 2 * ((p >> 4) & 1) + ((p >> 3) & 1); }
+QWZ_DEVINL int vt_dim(int l) { return (l >> 2) + 8 * (l & 1) + 16 * ((l >> 1) & 1); }
+
+// One block's 32 codes (words w after transpose8) as 16 f16x2 words in the
+// tile order, (c - 2^(b-1) + 0.5) * s / 2^(b-1): one fma.rn.f16x2 per pair
+// when s / 2^(b-1) and half of it are normal FP16 numbers (or s is 0), the
+// FP32 reader otherwise.
+template <int BITS>
+QWZ_DEVINL void block_values(const uint32_t (&w)[8], uint32_t hscale, uint32_t (&r)[16]) {
+  constexpr uint32_t kMin = BITS == 8 ? kKFastMin : kVFastMin;
+  constexpr uint32_t kBase = BITS == 8 ? 0x64806480u : 0x64086408u;  // 1024 + 2^(b-1)
+  constexpr uint32_t kF = BITS == 8 ? 0x20002000u : 0x30003000u;     // 2^-(b-1)
+  constexpr uint32_t kH = BITS == 8 ? 0x1C001C00u : 0x2C002C00u;     // 2^-b
+  if (hscale == 0u || (hscale >= kMin && hscale < kHalfInf)) {
+    const uint32_t pr = __byte_perm(hscale, hscale, 0x1010);
+    const uint32_t s2 = hmul2_bits(pr, kF), hs2 = hmul2_bits(pr, kH);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      r[2 * j] = deq_h2(codes_h2(w[j], 0x4140u), kBase, s2, hs2);
+      r[2 * j + 1] = deq_h2(codes_h2(w[j], 0x4342u), kBase, s2, hs2);
+    }
+  } else {
+    const float mid = BITS == 8 ? 127.5f : 7.5f;
+    const float sm = half_bits_to_float(hscale) * (BITS == 8 ? (1.f / 128.f) : 0.125f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t x = w[j];
+      r[2 * j] = pack_half2(deq(x & 0xff, mid, sm), deq((x >> 8) & 0xff, mid, sm));
+      r[2 * j + 1] = pack_half2(deq((x >> 16) & 0xff, mid, sm), deq(x >> 24, mid, sm));
+    }
+  }
+}
+
+}  // namespace k8v4
+
+// The K8/V4 cache in the tcgen05 verify kernel: a K tile is two 128-byte-
+// swizzled boxes of bit planes (blocks 0-3 and 4-7 of the head) and one box
+// of FP16 scales (34 KB), a V tile one swizzled box of planes and one of
+// scales (18 KB); two tiles of each in flight.  A math thread owns whole
+// blocks of its token, so it transposes the bit planes of a block at once
+// and hands the values in the tile order of vt_pos; Q is rotated and laid out
+// in the same order, and O^T's rows come back to the head's order in the
+// epilogue.
+struct VtK8v4 {
+  static constexpr int kKStages = 2, kVStages = 2;
+  static constexpr int kKStage = 2 * k8v4::kKHalf + k8v4::kSBox;
+  static constexpr int kVStage = k8v4::kVBox + k8v4::kSBox;
+  static constexpr bool kRotated = true;
+  static constexpr int kBlocksPerPart = k8v4::kBlocks / kVtParts;
+
+  QWZ_DEVINL static void issue(bool is_k, const SplitParams& p, uint32_t dst, int kvh, int y, uint32_t bar) {
+    if (is_k) {
+      tma_load_2d(dst, &p.tm_kc, kvh * 256, y, bar);
+      tma_load_2d(dst + k8v4::kKHalf, &p.tm_kc, kvh * 256 + 128, y, bar);
+      tma_load_2d(dst + 2 * k8v4::kKHalf, &p.tm_ks, kvh * 16, y, bar);
+    } else {
+      tma_load_2d(dst, &p.tm_vc, kvh * 128, y, bar);
+      tma_load_2d(dst + k8v4::kVBox, &p.tm_vs, kvh * 16, y, bar);
+    }
+  }
+  template <class Put>
+  QWZ_DEVINL static void dequant_k(uint32_t st, int tt, int u, Put put) {
+#pragma unroll
+    for (int c = 0; c < kBlocksPerPart; ++c) {
+      const int b = kBlocksPerPart * u + c;
+      const uint32_t half = st + (b >> 2) * k8v4::kKHalf;
+      const int c0 = 2 * (b & 3);
+      const uint4 a0 = lds128(half + swz128(tt, c0)), a1 = lds128(half + swz128(tt, c0 + 1));
+      uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      k8v4::transpose8(w);
+      uint32_t r[16];
+      k8v4::block_values<8>(w, lds16(st + 2 * k8v4::kKHalf + tt * 16 + 2 * b), r);
+      put(b, r);
+    }
+  }
+  template <class Put>
+  QWZ_DEVINL static void dequant_v(uint32_t st, int tt, int u, bool zero, Put put) {
+#pragma unroll
+    for (int c = 0; c < kBlocksPerPart; ++c) {
+      const int b = kBlocksPerPart * u + c;
+      const uint4 a = lds128(st + swz128(tt, b));
+      uint32_t w[8] = {a.x, a.y, a.z, a.w, 0u, 0u, 0u, 0u};
+      k8v4::transpose8(w);
+      uint32_t r[16];
+      k8v4::block_values<4>(w, zero ? 0u : lds16(st + k8v4::kVBox + tt * 16 + 2 * b), r);
+      put(b, r);
+    }
+  }
+  // Q_rot rows of this KV head (R q per block: the butterfly when h32 is the
+  // natural-order Hadamard matrix, else 32 multiply-adds), each scaled by a
+  // power of two, FP16, at K position 32 b + vt_pos(p) of the K-major atoms.
+  template <typename T, int N>
+  QWZ_DEVINL static void stage(const SplitParams& p, int kvh, uint32_t qbase, float* rowfac, bool had, int mw,
+                               int lane) {
+    using namespace k8v4;
+    float rrow[kBlock];
+    if (!had) {
+#pragma unroll
+      for (int jj = 0; jj < kBlock; ++jj) rrow[jj] = __ldg(p.h32 + lane * kBlock + jj);
+    }
+    const int pos = vt_pos(lane);
+    for (int r = mw; r < N; r += kVtMathWarps) {
+      const int qi = r / kGroup, hg = r - qi * kGroup;
+      float xr[kBlocks];
+      float amax = 0.f;
+      if (qi < p.q_len) {
+        const T* row = reinterpret_cast<const T*>(p.q) + ((size_t)qi * kQHeads + kvh * kGroup + hg) * kHeadDim;
+#pragma unroll
+        for (int b = 0; b < kBlocks; ++b) {
+          const unsigned short raw = reinterpret_cast<const unsigned short*>(row)[b * kBlock + lane];
+          xr[b] = InTraits<T>::to_float2((uint32_t)raw).x;
+        }
+        if (had) {
+#pragma unroll
+          for (int b = 0; b < kBlocks; ++b) {
+            float x = xr[b];
+#pragma unroll
+            for (int stp = 1; stp < kBlock; stp <<= 1) {
+              const float o = __shfl_xor_sync(0xffffffffu, x, stp);
+              x = (lane & stp) ? o - x : x + o;
+            }
+            xr[b] = x * kInvSqrt32;
+          }
+        } else {
+          float xin[kBlocks];
+#pragma unroll
+          for (int b = 0; b < kBlocks; ++b) {
+            xin[b] = xr[b];
+            xr[b] = 0.f;
+          }
+#pragma unroll
+          for (int jj = 0; jj < kBlock; ++jj)
+#pragma unroll
+            for (int b = 0; b < kBlocks; ++b) xr[b] = fmaf(rrow[jj], __shfl_sync(0xffffffffu, xin[b], jj), xr[b]);
+        }
+#pragma unroll
+        for (int b = 0; b < kBlocks; ++b) amax = fmaxf(amax, fabsf(xr[b]));
+      } else {
+#pragma unroll
+        for (int b = 0; b < kBlocks; ++b) xr[b] = 0.f;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float sc = pow2_row_scale(amax);
+#pragma unroll
+      for (int b = 0; b < kBlocks; ++b) {
+        const int dl = b * kBlock + pos;  // K position of this lane's dim
+        const uint32_t addr = qbase + (dl >> 6) * (N * 128) + r * 128 + ((((dl & 63) >> 3) ^ (r & 7)) << 4) + (dl & 7) * 2;
+        const __half hv = __float2half_rn(xr[b] * sc);
+        asm volatile("st.shared.u16 [%0], %1;\n" ::"r"(addr), "h"(__half_as_ushort(hv)));
+      }
+      // padding rows (zero Q) keep a positive factor so masked scores stay -inf
+      if (lane == 0) rowfac[r] = qi < p.q_len ? p.sm_scale_log2 / sc : p.sm_scale_log2;
+    }
+  }
+  QWZ_DEVINL static bool rotation_check(const SplitParams& p, int tid) {
+    return __syncthreads_and(k8v4::h32_is_hadamard(p.h32, tid, kVtWarps * 32)) != 0;
+  }
+  QWZ_DEVINL static int o_dim(int d) { return (d & ~31) + k8v4::vt_dim(d & 31); }
+};
 
 template <typename T>
 static cudaError_t launch_k8v4_decode16_t(const SplitParams& p, cudaStream_t stream) {
@@ -957,8 +1014,8 @@ cudaError_t launch_k8v4_split(const SplitParams& p, int dtype, cudaStream_t stre
     if (dtype == kDtypeBF16) return launch_k8v4_decode16_t<__nv_bfloat16>(p, stream);
     return launch_k8v4_decode16_t<__half>(p, stream);
   }
-  if (dtype == kDtypeBF16) return launch_k8v4_split_t<__nv_bfloat16>(p, nt, stream);
-  return launch_k8v4_split_t<__half>(p, nt, stream);
+  if (dtype == kDtypeBF16) return launch_verify_tc<__nv_bfloat16, VtK8v4>(p, stream);
+  return launch_verify_tc<__half, VtK8v4>(p, stream);
 }
 
 cudaError_t launch_k8v4_append(const K8v4AppendParams& p, int dtype, cudaStream_t stream) {
