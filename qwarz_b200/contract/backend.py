@@ -36,15 +36,11 @@ DECODE_POLICY = {
     "draft": {"kernel": "fp8_draft_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
               "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37},
     "combine": {"kernel": "lse_combine_kernel", "threads": 256, "split_groups": 8},
-    "k8v4_q1": {"kernel": "k8v4_decode16_kernel", "warps": 17,
-                "roles": "two groups of 8 (even / odd 128-token stages), one TMA producer",
-                "stage_tokens": 128, "stages": 4, "mma": "mma.sync m16n8k16 tokens x heads(6->8)",
-                "dequant": "bit planes -> FP16 by rotate/merge and fma.rn.f16x2", "ctas_per_sm": 1},
-    "k8v4_q2-8": {"kernel": "verify_tc_kernel<VtK8v4>", "warps": 19,
-                  "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
-                  "stage_tokens": 128, "stages": {"K": 2, "V": 2},
-                  "dequant": "8x8 bit transpose per (token, 32-dim block), fma.rn.f16x2",
-                  "mma": "tcgen05 kind::f16 M=128 as the NVFP4 verify"},
+    "k8v4": {"kernel": "verify_tc_kernel<VtK8v4> (q_len 1..8)", "warps": 19,
+             "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
+             "stage_tokens": 128, "stages": {"K": 2, "V": 2},
+             "dequant": "8x8 bit transpose per (token, 32-dim block), fma.rn.f16x2",
+             "mma": "tcgen05 kind::f16 M=128 as the NVFP4 verify"},
     "k8v4_combine": {"kernel": "lse_combine_kernel (rotate mode)", "threads": 256, "out": "R^T O per 32 dims"},
 }
 

@@ -37,8 +37,6 @@ bool is_split_kernel(const void* f) {
       reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 16, VtK8v4>),
       reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 32, VtK8v4>),
       reinterpret_cast<const void*>(verify_tc_kernel<__nv_bfloat16, 48, VtK8v4>),
-      reinterpret_cast<const void*>(k8v4_decode16_kernel<__half>),
-      reinterpret_cast<const void*>(k8v4_decode16_kernel<__nv_bfloat16>),
   };
   for (const void* k : known)
     if (k == f) return true;
