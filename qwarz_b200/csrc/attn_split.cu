@@ -7,9 +7,10 @@
 //   q_len 1     nvfp4_decode_kernel (attn_decode.cu): page-streamed by TMA,
 //               dequantised in registers into mma.sync fragments (tokens on
 //               M, the 6 GQA heads on N);
-//   q_len 2..8  nvfp4_verify_tc_kernel (attn_verify_tc.cu): 128-token tiles
-//               by TMA, K and V^T dequantised into tensor memory, QK and PV
-//               on tcgen05 with accumulators in tensor memory.
+//   q_len 2..8  verify_tc_kernel<VtNvfp4> (attn_verify_tc.cu): 128-token
+//               tiles by TMA, K dequantised into tensor memory and V into
+//               shared memory, QK and PV on tcgen05 with accumulators in
+//               tensor memory.
 //
 // Both write partials (m, l, O) with O unnormalised and m in log2 units of
 // sm_scale * q.k, merged by lse_combine_kernel (attn_combine.cu); the online
