@@ -76,7 +76,10 @@ def quantize_blocks(x_rot: np.ndarray, bits: int) -> tuple[np.ndarray, np.ndarra
     m = np.float32(1 << (bits - 1))
     with np.errstate(divide="ignore", invalid="ignore"):
         u = (x_rot / s) * m + m
-    c = np.clip(np.floor(np.nan_to_num(u, nan=0.0, posinf=0.0, neginf=0.0)), 0, (1 << bits) - 1)
+    # NaN codes as 0 and +-inf saturate, as the device's float-to-integer
+    # conversion and clamp do
+    c = np.clip(np.floor(np.nan_to_num(u, nan=0.0, posinf=np.float32(1e30), neginf=np.float32(-1e30))), 0,
+                (1 << bits) - 1)
     c = np.where(s > 0, c, m)
     return c.astype(np.uint8), s16
 

@@ -285,7 +285,6 @@ QWZ_DEVINL void sts64(uint32_t addr, uint32_t a, uint32_t b) {
 struct VtNvfp4 {
   static constexpr int kKStages = kVtKStages, kVStages = kVtVStages;
   static constexpr int kKStage = kVtHalfStage, kVStage = kVtHalfStage;
-  static constexpr bool kRotated = false;
   QWZ_DEVINL static void issue(bool is_k, const SplitParams& p, uint32_t dst, int kvh, int y, uint32_t bar) {
     tma_load_2d(dst, is_k ? &p.tm_kc : &p.tm_vc, kvh * kCodeBytes, y, bar);
     tma_load_2d(dst + kVtCodeBox, is_k ? &p.tm_ks : &p.tm_vs, kvh * kScaleBytes, y, bar);

@@ -122,7 +122,8 @@ QWZ_DEVINL int page_of(const int32_t* table, int width, int num_pages, int t) {
 template <typename T>
 __global__ void __launch_bounds__(512) k8v4_append_kernel(K8v4AppendParams p) {
   using namespace k8v4;
-  griddep_wait();
+  griddep_wait();               // the rows and the length may come from the previous kernel
+  griddep_launch_dependents();  // the split may begin its launch (it waits for this grid to finish)
   const int s = blockIdx.x, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool is_v = warp >= kBlocks;
@@ -276,7 +277,6 @@ struct VtK8v4 {
   static constexpr int kKStages = 2, kVStages = 2;
   static constexpr int kKStage = 2 * k8v4::kKHalf + k8v4::kSBox;
   static constexpr int kVStage = k8v4::kVBox + k8v4::kSBox;
-  static constexpr bool kRotated = true;
   static constexpr int kBlocksPerPart = k8v4::kBlocks / kVtParts;
 
   QWZ_DEVINL static void issue(bool is_k, const SplitParams& p, uint32_t dst, int kvh, int y, uint32_t bar) {
