@@ -341,3 +341,38 @@ def test_k8v4_slot_called_with_packed_arguments(cuda, q_len, split_len, splits):
     assert _lib.device_error(clear=True) == 0
     ref = ok8.attention(q.cpu(), c, table, pre)
     assert_close_rotated(out.float().cpu().numpy(), ref.numpy(), f"packed k8v4 q_len={q_len}")
+
+
+def test_full_size_properties(cuda):
+    """131,072 tokens (config 3's long context) written by the device writer:
+    a repeated call is bit-identical, and so is the same sequence stored in
+    another physical page order (the pages copied through a permutation and
+    the table remapped), for q_len 1 and 7."""
+    import bench
+    from qwarz_b200 import _lib, k8v4, ops
+
+    T = 131072
+    P = T // 256
+    cache, table = bench.k8v4_layer(cuda, P, T, 123)
+    perm = torch.randperm(P, generator=torch.Generator(device=cuda).manual_seed(9), device=cuda)
+    moved = tuple(torch.empty_like(t) for t in cache)
+    for src, dst in zip(cache, moved):
+        dst[perm.long()] = src  # physical page p of the copy holds page perm^-1 ...
+    table2 = perm[table.long()].to(torch.int32)  # ... so logical page i now lives at perm[table[i]]
+    h32 = k8v4.hadamard32(cuda)
+    for q_len in (1, 7):
+        q = torch.randn(q_len, 24, 256, generator=torch.Generator(device=cuda).manual_seed(q_len), device=cuda).bfloat16()
+        lens = torch.tensor([T - q_len], dtype=torch.int32, device=cuda)
+        splits = ops.default_splits(cuda, T, q_len)
+        po, pml = ops.split_workspace(cuda, q_len, splits)
+        outs = []
+        for c, t in ((cache, table), (cache, table), (moved, table2)):
+            out = torch.empty_like(q)
+            k8v4.split(q, c, t, lens, po, pml, h32, splits)
+            k8v4.combine(po, pml, out, h32, splits)
+            outs.append(out)
+        torch.cuda.synchronize()
+        assert torch.isfinite(outs[0].float()).all()
+        assert torch.equal(outs[0], outs[1]), f"repeated call q_len={q_len}"
+        assert torch.equal(outs[0], outs[2]), f"page order q_len={q_len}"
+    assert _lib.device_error(clear=True) == 0
