@@ -38,6 +38,7 @@
 // that left.
 
 #include "attn_common.cuh"
+#include "nvfp4_quant.cuh"
 #include "tc_common.cuh"
 
 namespace qwz {
@@ -304,6 +305,21 @@ struct VtNvfp4 {
   }
   QWZ_DEVINL static bool rotation_check(const SplitParams&, int) { return true; }
   QWZ_DEVINL static int o_dim(int d) { return d; }  // the V tile's d order is the head's
+  // The fused append: new row s (at logical position pos) of K (tensor 0)
+  // or V (1) for KV head kvh, quantised by one warp into the pool and fenced
+  // for the TMA reads that follow (the rule of nvfp4_append_kernel).
+  template <typename T>
+  QWZ_DEVINL static void append_row(const SplitParams& p, int pos, int s, int kvh, int tensor, int lane) {
+    const int pp = lookup_page(p, pos, lane == 0 && tensor == 0);
+    if (pp < 0) return;
+    const size_t row = ((size_t)pp * kPage + (pos & (kPage - 1))) * kKvHeads + kvh;
+    const T* src = reinterpret_cast<const T*>(tensor ? p.app_v : p.app_k) + ((size_t)s * kKvHeads + kvh) * kHeadDim;
+    uint8_t* codes = const_cast<uint8_t*>(tensor ? p.v_codes : p.k_codes) + row * kCodeBytes;
+    uint8_t* scales = const_cast<uint8_t*>(tensor ? p.v_scales : p.k_scales) + row * kScaleBytes;
+    quant::quantize_row_lane<T>(src, codes, scales, lane);
+    __threadfence();
+    fence_proxy_async_global();
+  }
 };
 
 template <typename T, int N, class F>
@@ -365,6 +381,16 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
   }
   const bool had = F::rotation_check(p, tid);  // the K8/V4 rotation test (a CTA-wide barrier)
+  if (p.app_k != nullptr && warp >= kVtMath0) {
+    // fused append: the q_len new rows that fall in this CTA's tiles, one
+    // warp per (row, K or V), written and fenced before any tile is loaded
+    const int first = p.tok_begin + rg.st_lo * kPage, last = first + rg.n_st * kPage;
+    const int pre = len_all - p.len_add;
+    for (int task = warp - kVtMath0; task < 2 * p.q_len; task += kVtMathWarps) {
+      const int srow = task >> 1, pos = pre + srow;
+      if (pos >= first && pos < last) F::template append_row<T>(p, pos, srow, kvh, task & 1, lane);
+    }
+  }
   if (warp >= kVtMath0) {
     F::template stage<T, N>(p, kvh, sb + L::kQ, rowfac, had, warp - kVtMath0, lane);
     fence_proxy_async_smem();  // Q is read by the tensor core

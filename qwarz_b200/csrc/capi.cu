@@ -307,17 +307,12 @@ int qwz_nvfp4_attend(const void* q, const void* k, const void* v, void* k_cache,
   rc = fill_split(p, q, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
                   partial_o, partial_ml, table_width, num_pages, q_len, num_splits, 0, sm_scale);
   if (rc) return rc;
-  if (q_len == 1) {  // the decode kernel writes the new row itself (one launch fewer)
-    if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
-      return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
-    p.app_k = k;
-    p.app_v = v;
-  } else {
-    rc = qwz_nvfp4_append(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
-                          table_width, q_len, qwz::kKvHeads, qwz::kPage, qwz::kHeadDim, num_pages,
-                          dtype, stream);
-    if (rc) return rc;
-  }
+  // the split kernel (decode or verify) writes the new rows itself, in the
+  // CTAs whose pages hold them, before it reads those pages (one launch fewer)
+  if (!k || !v || !aligned(k, 16) || !aligned(v, 16))
+    return fail(QWZ_EINVAL, "k and v must be non-null 16-byte aligned pointers");
+  p.app_k = k;
+  p.app_v = v;
   rc = launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_nvfp4_attend(split)");
   if (rc) return rc;
   const qwz::CombineParams c =
@@ -600,14 +595,9 @@ int qwz_attn_shard_split(const void* q, const void* k, const void* v, void* k_ca
   p.tok_begin = tok_begin;
   p.tok_span = tok_span;
   p.table_page_offset = tok_begin / qwz::kPage;
-  if (q_len == 1) {  // the shard that owns the new row's page writes it inside the decode kernel
-    p.app_k = k;
-    p.app_v = v;
-  } else {
-    rc = qwz_nvfp4_append_shard(k, v, k_cache, v_cache, k_scales, v_scales, block_table, cache_seqlens,
-                                table_width, tok_begin / qwz::kPage, q_len, num_pages, dtype, stream);
-    if (rc) return rc;
-  }
+  // the shard that owns a new row's page writes it inside the split kernel
+  p.app_k = k;
+  p.app_v = v;
   return launched(qwz::launch_nvfp4_split(p, dtype, as_stream(stream)), "qwz_attn_shard_split");
 }
 

@@ -388,6 +388,9 @@ struct VtK8v4 {
     return __syncthreads_and(k8v4::h32_is_hadamard(p.h32, tid, kVtWarps * 32)) != 0;
   }
   QWZ_DEVINL static int o_dim(int d) { return (d & ~31) + k8v4::vt_dim(d & 31); }
+  // rows are appended by qwz_k8v4_append (the split is never given app_k)
+  template <typename T>
+  QWZ_DEVINL static void append_row(const SplitParams&, int, int, int, int, int) {}
 };
 
 cudaError_t launch_k8v4_split(const SplitParams& p, int dtype, cudaStream_t stream) {
