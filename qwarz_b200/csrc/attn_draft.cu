@@ -6,7 +6,9 @@
 // shadow store, engine/forward/draft.py:266-296), with an optional FP32
 // scale per (256-token page, KV head); the reference's scale is 1.
 //
-// Pipeline as in attn_decode.cu: CTA = one KV head x one split, 8 warps;
+// Pipeline as in attn_decode.cu: CTA = one KV head x one split (or, when
+// the splits are too few to give every SM a CTA, one share of a split whose
+// cluster of CTAs merges through distributed shared memory), 8 warps;
 // each 128-token stage arrives by TMA as four boxes (K and V, head-dim halves
 // d < 128 and d >= 128, [128 tokens x 128 B] with the 128-byte swizzle; 64 KB)
 // into a 3-deep ring; the last warp to release a slot issues the next stage
@@ -123,10 +125,132 @@ QWZ_DEVINL void issue_stage(const SplitParams& p, DrMeta* meta, const StageRange
   tma_load_2d(dst + 3 * kDrHalf, &p.tm_vc, x + 128, t0, fb);
 }
 
+// ---------------------------------------------------------------- clusters
+QWZ_DEVINL int cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return (int)r;
+}
+QWZ_DEVINL int cluster_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(r));
+  return (int)r;
+}
+// Every thread of every CTA of the cluster; orders the shared-memory writes
+// before the barrier with the peers' reads after it.
+QWZ_DEVINL void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+QWZ_DEVINL float ld_peer_f32(const float* local, int rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(a) : "memory");
+  return v;
+}
+
+// The cluster form of decode_epilogue: a chunk (split) is streamed by the
+// csize CTAs of one cluster, each over a contiguous share of its stages.
+// Each CTA merges its warps (the same fixed-order rule) into an (M, l, O)
+// record in its own shared memory; rank 0 then merges the ranks' records
+// in rank order (weights exp2(M_r - M), 0 for an empty share) through
+// distributed shared memory and stores the chunk's partial.
+constexpr int kDrMaxCluster = 4;
+constexpr int kDrEpiBytes = (epilogue_smem_bytes(kDrWarps) + 15) / 16 * 16;  // then the cluster record
+template <int WARPS, class DInv>
+QWZ_DEVINL void draft_epilogue_cluster(const SplitParams& p, uint8_t* smem, int split, int kvh, int crank,
+                                       int csize, float m0, float m1, float l0, float l1,
+                                       const float (&o)[16][4], DInv dinv) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += shfl_xor(l0, off);
+    l1 += shfl_xor(l1, off);
+  }
+  float4* red = reinterpret_cast<float4*>(smem);                       // [WARPS][16][33]
+  float* mlred = reinterpret_cast<float*>(red + WARPS * 16 * kEpiRowF4);  // [WARPS][8][2]
+  float* wts = mlred + WARPS * 16;                                      // [8 cols][WARPS]
+  static_assert(WARPS == kDrWarps, "the record follows the draft kernel's epilogue area");
+  float* ofin = reinterpret_cast<float*>(smem + kDrEpiBytes);           // [6][256]
+  float* mlfin = ofin + kGroup * kHeadDim;                              // [6][2]
+  float* wfin = mlfin + 2 * kGroup;                                     // [6][kDrMaxCluster]
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    red[(warp * 16 + j) * kEpiRowF4 + lane] = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
+  if (g == 0) {
+    mlred[(warp * 8 + 2 * qd) * 2 + 0] = m0;
+    mlred[(warp * 8 + 2 * qd) * 2 + 1] = l0;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 0] = m1;
+    mlred[(warp * 8 + 2 * qd + 1) * 2 + 1] = l1;
+  }
+  __syncthreads();
+  if (tid < kGroup) {
+    const int col = tid;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, mlred[(w * 8 + col) * 2]);
+    float ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) {
+      const float mw = mlred[(w * 8 + col) * 2];
+      const float wt = (mw == -CUDART_INF_F) ? 0.f : exp2_approx(mw - M);
+      wts[col * WARPS + w] = wt;
+      ls += wt * mlred[(w * 8 + col) * 2 + 1];
+    }
+    mlfin[2 * col] = M;
+    mlfin[2 * col + 1] = ls;
+  }
+  __syncthreads();
+  const float* rf = reinterpret_cast<const float*>(red);
+  for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
+    const int col = idx >> 8, d = idx & 255;
+    int gg, j;
+    dinv(d, gg, j);
+    const int src = ((j * kEpiRowF4) + 4 * gg + (col >> 1)) * 4 + (col & 1) + 2 * (d & 1);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) acc += wts[col * WARPS + w] * rf[w * 16 * kEpiRowF4 * 4 + src];
+    ofin[idx] = acc;
+  }
+  cluster_sync();  // every rank's record is in its shared memory
+  if (crank == 0) {
+    if (tid < kGroup) {
+      const int col = tid;
+      float mr[kDrMaxCluster];
+      float M = -CUDART_INF_F;
+      for (int r = 0; r < csize; ++r) {
+        mr[r] = r == 0 ? mlfin[2 * col] : ld_peer_f32(mlfin + 2 * col, r);
+        M = fmaxf(M, mr[r]);
+      }
+      float ls = 0.f;
+      for (int r = 0; r < csize; ++r) {
+        const float wt = (mr[r] == -CUDART_INF_F) ? 0.f : exp2_approx(mr[r] - M);
+        wfin[col * kDrMaxCluster + r] = wt;
+        ls += wt * (r == 0 ? mlfin[2 * col + 1] : ld_peer_f32(mlfin + 2 * col + 1, r));
+      }
+      const size_t base = (size_t)(kvh * kGroup + col) * p.num_splits + split;
+      p.partial_ml[base * 2 + 0] = M;
+      p.partial_ml[base * 2 + 1] = ls;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < kGroup * kHeadDim; idx += blockDim.x) {
+      const int col = idx >> 8, d = idx & 255;
+      float acc = wfin[col * kDrMaxCluster] * ofin[idx];
+      for (int r = 1; r < csize; ++r) acc += wfin[col * kDrMaxCluster + r] * ld_peer_f32(ofin + idx, r);
+      const size_t base = (size_t)(kvh * kGroup + col) * p.num_splits + split;
+      p.partial_o[base * kHeadDim + d] = acc;
+    }
+  }
+  cluster_sync();  // a peer's shared memory stays until rank 0 has read it
+}
+
 }  // namespace
 
 // Launched with programmatic stream serialisation: barriers are set up while
 // the previous kernel drains, global memory is read after griddep_wait().
+// kCluster: the grid's x is split x cluster size, and the CTAs of a cluster
+// share the split's stages (contiguous shares, merged in the epilogue).
+template <bool kCluster>
 __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __grid_constant__ SplitParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sraw = smem_u32(smem);
@@ -135,7 +259,8 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
   const uint32_t bar_full = sbase + kDrStages * kDrStageBytes;
   DrMeta* meta = reinterpret_cast<DrMeta*>(sgen + kDrStages * kDrStageBytes + 8 * kDrStages);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int crank = kCluster ? cluster_rank() : 0, csize = kCluster ? cluster_size() : 1;
+  const int split = blockIdx.x / csize, kvh = blockIdx.y;
 
   if (tid == 0) {
 #pragma unroll
@@ -147,15 +272,20 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
     mbar_fence_init();
   }
   griddep_wait();  // shared-memory set-up overlaps the previous kernel
-  const StageRange rg = stage_range<kDrTokens>(p, split);
+  StageRange rg = stage_range<kDrTokens>(p, split);
+  if (kCluster) {  // this rank's contiguous share of the split's stages
+    const int a = rg.n_st * crank / csize, b = rg.n_st * (crank + 1) / csize;
+    rg.st_lo += a;
+    rg.n_st = b - a;
+  }
   int slot_new = -1;  // fused shadow write: the store slot, while a stage of this CTA may hold it
   if (p.app_k != nullptr) {
     slot_new = __ldg(p.app_slot);
     if (slot_new < 0 || slot_new >= p.capacity) {
-      if (split == 0 && kvh == 0 && tid == 0) flag_error(kErrSlotRange);
+      if (split == 0 && crank == 0 && kvh == 0 && tid == 0) flag_error(kErrSlotRange);
       slot_new = -1;
     } else if (slot_new >= rg.tok_end) {  // past the attended keys: split 0 writes the store only
-      if (split == 0 && warp == 0) {
+      if (split == 0 && crank == 0 && warp == 0) {
         const int pg = slot_new >> 8;
         fp8_shadow_patch(p, slot_new, kvh, lane, p.k_page_scale ? __ldg(p.k_page_scale + pg * kKvHeads + kvh) : 1.f,
                          p.v_page_scale ? __ldg(p.v_page_scale + pg * kKvHeads + kvh) : 1.f, 0u, 0);
@@ -294,18 +424,65 @@ __global__ void __launch_bounds__(kDrWarps * 32, 1) fp8_draft_kernel(const __gri
   }
   __syncthreads();
   griddep_launch_dependents();
-  decode_epilogue<kDrWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, [](int d, int& gg, int& j) {
+  auto dinv = [](int d, int& gg, int& j) {
     gg = (d & 127) >> 4;
     j = ((d >> 7) << 3) + ((d & 15) >> 1);
-  });
+  };
+  if constexpr (kCluster)
+    draft_epilogue_cluster<kDrWarps>(p, smem, split, kvh, crank, csize, m0, m1, l0, l1, o, dinv);
+  else
+    decode_epilogue<kDrWarps>(p, smem, split, kvh, m0, m1, l0, l1, o, dinv);
 }
 
+namespace {
+
+int sm_count_of_current_device() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] == 0) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cached[dev];
+}
+
+}  // namespace
+
+// With fewer chunks than the SMs can hold (the reference's 16 chunks are 64
+// CTAs on 148 SMs), each chunk is streamed by a cluster of up to four CTAs,
+// so every SM pulls pages; the chunk count, the workspace and the combine
+// are unchanged.
 cudaError_t launch_fp8_split(const SplitParams& p, cudaStream_t stream) {
-  static_assert(epilogue_smem_bytes(kDrWarps) <= kDrStages * kDrStageBytes, "epilogue reuses the ring");
-  cudaError_t e = cudaFuncSetAttribute(fp8_draft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static_assert(kDrEpiBytes + 4 * (kGroup * kHeadDim + 2 * kGroup + kGroup * kDrMaxCluster) <=
+                    kDrStages * kDrStageBytes,
+                "epilogue reuses the ring");
+  const int sms = sm_count_of_current_device();
+  int cl = sms > 0 ? sms / (p.num_splits * kKvHeads) : 1;
+  cl = cl < 1 ? 1 : (cl > kDrMaxCluster ? kDrMaxCluster : cl);
+  if (cl == 3) cl = 2;  // cluster sizes that tile a GPC's SM pairs
+  if (cl == 1) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_draft_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kDrSmemBytes);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(fp8_draft_kernel<false>, dim3(p.num_splits, kKvHeads), dim3(kDrWarps * 32), kDrSmemBytes,
+                      stream, p);
+  }
+  cudaError_t e = cudaFuncSetAttribute(fp8_draft_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kDrSmemBytes);
   if (e != cudaSuccess) return e;
-  return launch_pdl(fp8_draft_kernel, dim3(p.num_splits, kKvHeads), dim3(kDrWarps * 32), kDrSmemBytes, stream, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.num_splits * cl, kKvHeads);
+  cfg.blockDim = dim3(kDrWarps * 32);
+  cfg.dynamicSmemBytes = kDrSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cl;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, fp8_draft_kernel<true>, p);
 }
 
 }  // namespace qwz
