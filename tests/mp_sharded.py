@@ -1,8 +1,10 @@
 """Run by tests/test_gpu_multi.py under torch.distributed.run, one process
 per GPU: the sequence-sharded decode (ShardedDecode) with the peer-memory
 exchange and with NCCL, eager and replayed from a CUDA graph, against the
-FP32 oracle over the whole sequence.  Prints one JSON line per rank and exits
-non-zero on a mismatch."""
+FP32 oracle over the whole sequence; then the MTP7 verify over the peer
+exchange with its 7 new rows across the shard boundary at token 2048 (the
+owners write them inside their verify kernels).  Prints one JSON line per
+rank and exits non-zero on a mismatch."""
 from __future__ import annotations
 
 import json
@@ -37,24 +39,25 @@ def main() -> int:
     shard = sharded.shard_pages(pages, world)[rank]
     phys = table[shard.first_page:shard.first_page + shard.num_pages]
     results = {}
-    for mode in ("peer", "nccl"):
+    for mode, q_len in (("peer", 1), ("nccl", 1), ("peer", 7)):
         d = {n: np.ascontiguousarray(c[n][phys]) for n in ("k_cache", "v_cache", "k_scales", "v_scales")}
         d["table"] = np.arange(shard.num_pages, dtype=np.int32)
         dc = to_device(d, device)
         cache = (dc["k_cache"], dc["v_cache"], dc["k_scales"], dc["v_scales"])
-        dec = sharded.ShardedDecode(shard, device, exchange=mode)
+        dec = sharded.ShardedDecode(shard, device, q_len=q_len, exchange=mode)
         refm = {n: v.copy() for n, v in ref.items()}
-        q = queries(31, 1, torch.bfloat16).to(device)
+        q = queries(31 if q_len == 1 else 41, q_len, torch.bfloat16).to(device)
         out = torch.empty_like(q)
         errs = []
         lens = torch.zeros(1, dtype=torch.int32, device=device)
-        kd = torch.empty(1, 4, 256, dtype=torch.bfloat16, device=device)
+        kd = torch.empty(q_len, 4, 256, dtype=torch.bfloat16, device=device)
         vd = torch.empty_like(kd)
         graph = None
+        start = total if q_len == 1 else 2045  # verify: rows 2045.. cross the page-8 shard boundary
         for step in range(4):  # steps 0-1 eager, 2-3 replayed from one CUDA graph
-            pre = total + step
-            kn = torch.from_numpy(cases.kv_rows(600 + step, 1)).to(torch.bfloat16)
-            vn = torch.from_numpy(cases.kv_rows(700 + step, 1)).to(torch.bfloat16)
+            pre = start + step
+            kn = torch.from_numpy(cases.kv_rows(600 + step, q_len)).to(torch.bfloat16)
+            vn = torch.from_numpy(cases.kv_rows(700 + step, q_len)).to(torch.bfloat16)
             nvfp4.append(kn.float().numpy(), vn.float().numpy(), refm["k_cache"], refm["v_cache"],
                          refm["k_scales"], refm["v_scales"], table, pre)
             lens.fill_(pre)
@@ -74,7 +77,8 @@ def main() -> int:
                                                                if k != "table"},
                                           block_table=torch.from_numpy(table), pre_len=pre)
             try:
-                assert_close_attention(out.float().cpu().numpy(), expect.numpy(), f"{mode} step {step}", "bfloat16")
+                assert_close_attention(out.float().cpu().numpy(), expect.numpy(), f"{mode} q_len {q_len} step {step}",
+                                       "bfloat16")
             except AssertionError as e:
                 errs.append(str(e))
             if graph is not None and step == 2:
@@ -83,7 +87,7 @@ def main() -> int:
                 pass
         del graph
         errs += [] if _lib.device_error(clear=True) == 0 else ["device error word set"]
-        results[mode] = errs or "ok"
+        results[f"{mode}_q{q_len}"] = errs or "ok"
         dec.close()
     torch.cuda.synchronize()
     dist.barrier()
