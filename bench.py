@@ -956,13 +956,14 @@ def run_profile_case(args, device) -> dict:
             k8v4.combine(po, pml, out, h32, splits)
         torch.cuda.synchronize()
         return {"workload": args.workload, "tokens": tokens, "ok": True}
-    if args.workload == "profile_draft":
+    if args.workload in ("profile_draft", "profile_draft16"):
         T = tokens + 6
         k8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
         v8 = torch.randn(1, T, KV_HEADS, DIM, generator=g, device=device).to(torch.float8_e4m3fn)
         q = torch.randn(1, 1, HEADS, DIM, generator=g, device=device).half()
         out = torch.empty_like(q)
-        attn = DecodeAttention(HEADS, KV_HEADS, DIM, device)
+        # profile_draft16: BASELINE's 16 chunks (each chunk a cluster of CTAs)
+        attn = DecodeAttention(HEADS, KV_HEADS, DIM, device, **({"splits": 16} if args.workload.endswith("16") else {}))
         length = torch.tensor([tokens], dtype=torch.int32, device=device)
         for _ in range(3):
             attn.attend(q, k8, v8, length, out)
@@ -1071,7 +1072,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--workload", default="auto",
                     choices=["auto", "c3", "c4", "c5", "k8v4", "prefill", "all", "profile_prefill",
-                             "profile_decode", "profile_verify", "profile_draft", "profile_k8v4"],
+                             "profile_decode", "profile_verify", "profile_draft", "profile_draft16",
+                             "profile_k8v4"],
                     help="auto: the driver's headline (config 2 at N=1 with sub-records, config 4 "
                          "split over the N GPUs at N>1); c3/c4/c5/k8v4/prefill/all: single-GPU configs "
                          "(separate JSON); profile_*: three eager launches of one kernel on one "
