@@ -186,14 +186,21 @@ QWZ_DEVINL void st_cols(uint32_t taddr, const float (&v)[NC]) {
 // of two (FP16-exact), and the per-row score factor sm_scale*log2e/scale.
 template <typename T, int N>
 QWZ_DEVINL void stage_q(const SplitParams& p, int kvh, uint32_t qbase, float* rowfac, int mw, int lane) {
-  for (int r = mw; r < N; r += kVtMathWarps) {
-    const int qi = r / kGroup, hg = r - qi * kGroup;
-    uint32_t w[4] = {0u, 0u, 0u, 0u};
-    if (qi < p.q_len) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) +
-                                                           ((size_t)qi * kQHeads + kvh * kGroup + hg) * kHeadDim) + lane);
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    }
+  constexpr int kRows = (N + kVtMathWarps - 1) / kVtMathWarps;  // rows of this warp
+  uint4 raw[kRows];
+#pragma unroll
+  for (int j = 0; j < kRows; ++j) {  // all loads first: one memory latency, not kRows
+    const int r = mw + j * kVtMathWarps, qi = r / kGroup, hg = r - qi * kGroup;
+    raw[j] = make_uint4(0u, 0u, 0u, 0u);
+    if (r < N && qi < p.q_len)
+      raw[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) +
+                                                    ((size_t)qi * kQHeads + kvh * kGroup + hg) * kHeadDim) + lane);
+  }
+#pragma unroll
+  for (int j = 0; j < kRows; ++j) {
+    const int r = mw + j * kVtMathWarps, qi = r / kGroup;
+    if (r >= N) break;
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -391,12 +398,8 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       if (pos >= first && pos < last) F::template append_row<T>(p, pos, srow, kvh, task & 1, lane);
     }
   }
-  if (warp >= kVtMath0) {
-    F::template stage<T, N>(p, kvh, sb + L::kQ, rowfac, had, warp - kVtMath0, lane);
-    fence_proxy_async_smem();  // Q is read by the tensor core
-  }
   tc::fence_before();
-  __syncthreads();
+  __syncthreads();  // barriers, the TMEM base, the page ids and appended rows are in place
   tc::fence_after();
   const uint32_t tbase = *tmem_slot;
 
@@ -509,6 +512,12 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       nm[c] = -kMFloor;
     }
     bool ok = true;
+
+    // Q while the producers' first tiles are in flight; QK(0) waits for
+    // kready(0), which every math warp arrives at only after staging its rows
+    F::template stage<T, N>(p, kvh, sb + L::kQ, rowfac, had, warp - kVtMath0, lane);
+    fence_proxy_async_smem();  // Q is read by the tensor core
+    math_bar();                // every row's score factor is written before a softmax reads it
 
     // K(j) -> TMEM, thread = token tt, head-dim part u (columns 16 g ..);
     // returns the tile's valid end, read before the ring slot is released
