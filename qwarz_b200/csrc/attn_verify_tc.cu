@@ -380,18 +380,22 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
   // barriers and tensor memory are set up while the previous kernel drains;
   // global memory (lengths, table, Q, pages) only after it completes
   griddep_wait();
-  const StageRange rg = stage_range<kPage>(p, split);
-  const int n_tiles = 2 * rg.n_st;
+  // tile-granular split bounds: a split may start or end mid-page, which
+  // evens out the splits (at 32K, 7 tiles at most instead of 4 pages = 8)
+  const StageRange rg = stage_range<kVtTile>(p, split);
+  const int n_tiles = rg.n_st;
+  const int page0 = rg.st_lo >> 1;  // this split's first page (pages from tok_begin)
+  const int n_pages = n_tiles > 0 ? ((rg.st_lo + n_tiles + 1) >> 1) - page0 : 0;
   const int len_all = __ldg(p.seqlens) + p.len_add;  // causal limits use the whole sequence
   if (warp == 0) {
-    for (int i = lane; i < min(rg.n_st, kVtPidCache); i += 32)
-      pid[i] = lookup_page(p, p.tok_begin + (rg.st_lo + i) * kPage, true);
+    for (int i = lane; i < min(n_pages, kVtPidCache); i += 32)
+      pid[i] = lookup_page(p, p.tok_begin + (page0 + i) * kPage, true);
   }
   const bool had = F::rotation_check(p, tid);  // the K8/V4 rotation test (a CTA-wide barrier)
   if (p.app_k != nullptr && warp >= kVtMath0) {
     // fused append: the q_len new rows that fall in this CTA's tiles, one
     // warp per (row, K or V), written and fenced before any tile is loaded
-    const int first = p.tok_begin + rg.st_lo * kPage, last = first + rg.n_st * kPage;
+    const int first = p.tok_begin + rg.st_lo * kVtTile, last = first + n_tiles * kVtTile;
     const int pre = len_all - p.len_add;
     for (int task = warp - kVtMath0; task < 2 * p.q_len; task += kVtMathWarps) {
       const int srow = task >> 1, pos = pre + srow;
@@ -424,8 +428,8 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
           *abort_flag = 1;
           break;
         }
-        const int k = i >> 1;
-        const int t0 = p.tok_begin + (rg.st_lo + k) * kPage + kVtTile * (i & 1);
+        const int gt = rg.st_lo + i, k = (gt >> 1) - page0;  // tile from tok_begin, page of this split
+        const int t0 = p.tok_begin + gt * kVtTile;
         const int pp = k < kVtPidCache ? pid[k] : lookup_page(p, t0, is_k);
         if (is_k) kstage_end[s] = pp >= 0 ? rg.tok_end : t0;  // released by the arrive below
         const uint32_t fb = full + 8 * s;
@@ -436,7 +440,7 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
         }
         mbar_arrive_expect_tx(fb, stage_bytes);
         const uint32_t dst = ring + s * stage_bytes;
-        const int y = pp * kPage + kVtTile * (i & 1);
+        const int y = pp * kPage + kVtTile * (gt & 1);
         F::issue(is_k, p, dst, kvh, y, fb);
       }
       // never leave with copies in flight (only reachable after an abort)
@@ -544,7 +548,7 @@ __global__ void __launch_bounds__(kVtWarps * 32, 1)
       const int sbuf = i & 1;
       ok &= mbar_wait(bar_s + 8 * sbuf, (i >> 1) & 1);
       tc::fence_after();
-      const int t0 = p.tok_begin + (rg.st_lo + (i >> 1)) * kPage + kVtTile * (i & 1);
+      const int t0 = p.tok_begin + (rg.st_lo + i) * kVtTile;
       const int vend = vend_next;
 
       float x[NP];
