@@ -32,9 +32,11 @@ DECODE_POLICY = {
              "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",
              "stage_tokens": 128, "stages": {"K": 3, "V": 2}, "copy": "TMA 2-D boxes, 128-byte swizzle",
              "mma": "tcgen05 kind::f16 M=128: S^T = K Q^T (K from TMEM, N=16/32/48), O^T = V^T P^T (FP16 P)",
-             "tmem_columns": 512, "ctas_per_sm": 1},
+             "tmem_columns": 512, "ctas_per_sm": 1, "split_bounds": "128-token tiles",
+             "append": "fused (the CTAs whose tiles hold the new rows) when called through qwz_nvfp4_attend"},
     "draft": {"kernel": "fp8_draft_kernel", "warps": 8, "stage_tokens": 128, "stages": 3,
-              "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37},
+              "copy": "TMA 2-D boxes, 128-byte swizzle", "splits": 37,
+              "clusters": "2 or 4 CTAs per chunk when chunks x 4 heads leave SMs idle (16 chunks: 2)"},
     "combine": {"kernel": "lse_combine_kernel", "threads": 256, "split_groups": 8},
     "k8v4": {"kernel": "verify_tc_kernel<VtK8v4> (q_len 1..8)", "warps": 19,
              "roles": "K TMA, MMA/TMEM owner, V TMA, 16 math (4 per TMEM lane quadrant)",

@@ -56,7 +56,8 @@ def build_contract() -> dict:
                 "q1": {"kernel": "nvfp4_decode_kernel", "stage_tokens": 256, "stages": 3,
                        "mma": "mma.sync m16n8k16", "mma_m": "16 tokens", "mma_n": "8 (6 GQA heads + 2 pad)",
                        "tokens_per_warp_per_stage": 32},
-                "q7": {"kernel": "nvfp4_verify_tc_kernel", "rows": 42, "stage_tokens": 128,
+                "q7": {"kernel": "verify_tc_kernel<VtNvfp4>", "rows": 42, "stage_tokens": 128,
+                       "split_bounds": "128-token tiles (a split may start or end mid-page)",
                        "mma": "tcgen05 kind::f16", "qk": "S^T[128 tokens x 48] = K Q^T, K in tensor memory",
                        "pv": "O^T[256 d x 48] += V^T P^T, two M=128 halves of d, V and P in shared memory"},
             },
